@@ -1,0 +1,405 @@
+"""Benchmark of the B200 onesweep radix sort (the headline of the metric
+"Onesweep sort Gkeys/s; scan/reduce HBM GB/s"), with scan, reduce and
+segment-reduce lines attached.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one "step"): DeviceRadixSort::SortPairs of n = 2^28 uint32 keys
+uniform over 2^32 with uint32 values = iota, per GPU.
+Inputs (2 GiB per step) are larger than L2 (126 MB), so no L2 flush is needed
+between sort steps; the reduce line (64 MiB input) flushes L2 between
+iterations.  Data: seeded PCG32 synthetic inputs.
+
+Under torchrun (N > 1) every rank sorts its own 2^28-pair shard (weak
+scaling); timings are the max over ranks.
+
+--impl reference times the reference algorithm's CPU path: the reference
+(LuisaCompute DSL kernels) cannot be built or run here, so this is the CPU
+restatement in oracle/ (multi-threaded LSD radix sort) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_SORT = 1 << 28
+METRIC = "Onesweep sort Gkeys/s; scan/reduce HBM GB/s (% of ~8 TB/s) at 1/2/4/8 B200"
+UNIT = "Gkeys/s"
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_gpu(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# ---------------------------------------------------------------------------
+def run_reference_arm(args, rank, world):
+    """CPU path of the reference algorithm on the host cores (rank 0 only)."""
+    if rank != 0:
+        return 0
+    import oracle
+    from lc_parallel_primitive_b200 import datagen as G
+
+    cores = os.cpu_count() or 1
+    sample = 1 << 24  # bounded sample of the 2^28-pair workload per step
+    keys = G.u32(sample, seed=1, stream=7)
+    vals = G.iota_u32(sample)
+    for _ in range(max(args.warmup, 1)):
+        oracle.radix_sort(keys, vals, threads=cores)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.radix_sort(keys, vals, threads=cores)
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    value = sample / sec / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u32", "data": "synthetic (PCG32 seeded)",
+        "config": {"workload": "SortPairs u32 keys (uniform 2^32) + u32 iota values, BASELINE config 3",
+                   "n_per_step": sample, "note": "reference CPU path = oracle/ LSD radix sort restatement "
+                   "(LuisaCompute, the reference's runtime, is absent: reference not buildable)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{sample} pairs per step (bounded sample of 2^28)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extras", action="store_true", help="skip the scan/reduce/segment lines")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+
+    import oracle  # checker and CPU baseline only
+    from lc_parallel_primitive_b200 import _lib as L
+    from lc_parallel_primitive_b200 import datagen as G
+    from lc_parallel_primitive_b200.primitives import CommandList, DeviceRadixSort, Stream, synchronize
+
+    lib = L.lib()
+    peak, peak_kind = load_peaks()
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+
+    # ---- inputs (host, pinned) ------------------------------------------------
+    n = N_SORT
+    keys_np = G.u32(n, seed=1 + rank, stream=7)
+    h_keys = torch.from_numpy(keys_np.view(np.int32)).pin_memory()
+    h_vals = torch.from_numpy(G.iota_u32(n).view(np.int32)).pin_memory()
+    h_keys_out = torch.empty_like(h_keys).pin_memory()
+    h_vals_out = torch.empty_like(h_vals).pin_memory()
+    d_keys = h_keys.to(dev)
+    d_vals = h_vals.to(dev)
+    d_keys_out = torch.empty_like(d_keys)
+    d_vals_out = torch.empty_like(d_vals)
+    tb = lib.lcpp_radix_sort_temp_bytes(L.U32, L.U32, n)
+    d_temp = torch.empty(tb, dtype=torch.uint8, device=dev)
+
+    def sort_once():
+        L.check(lib.lcpp_radix_sort(L.U32, L.U32, 0, d_keys.data_ptr(), d_keys_out.data_ptr(), d_vals.data_ptr(),
+                                    d_vals_out.data_ptr(), n, 0, 0, d_temp.data_ptr(), tb, sh), "sort")
+
+    for _ in range(args.warmup):
+        sort_once()
+    torch.cuda.synchronize()
+    L.check(lib.lcpp_last_device_error(sh), "device error")
+
+    # correctness of what is timed (size-independent properties on the device)
+    k = d_keys_out.view(torch.int32) ^ torch.tensor(-(1 << 31), dtype=torch.int32, device=dev)
+    assert bool((k[1:] >= k[:-1]).all()), "sort output not ordered"
+    perm_keys = d_keys.view(torch.int32)[d_vals_out.view(torch.int32).long()]
+    assert bool((perm_keys == d_keys_out.view(torch.int32)).all()), "values do not follow keys"
+    del k, perm_keys
+    torch.cuda.empty_cache()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- timed region: device-resident sort ---------------------------------
+    launches0 = lib.lcpp_kernel_launch_count()
+    lib.lcpp_profile_enable(1)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu(local_rank)) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            sort_once()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = start.elapsed_time(stop) / args.steps
+    launches = lib.lcpp_kernel_launch_count() - launches0
+    prof = {}
+    for kname in ("rs_memset", "rs_histogram", "rs_bins_scan", "rs_onesweep"):
+        c, t = L.C.c_uint64(0), L.C.c_double(0)
+        lib.lcpp_profile_read(kname.encode(), L.C.byref(c), L.C.byref(t))
+        prof[kname] = (int(c.value), float(t.value))
+    lib.lcpp_profile_enable(0)
+    ms = max_over_ranks(ms)
+    value = world * n / (ms * 1e-3) / 1e9
+
+    os_launches, os_ms = prof["rs_onesweep"]
+    os_avg_ms = os_ms / max(os_launches, 1)
+    os_bytes = 16 * n  # per pass: read key+value, write key+value (4 B each)
+    os_achieved = os_bytes / (os_avg_ms * 1e-3) / 1e9
+    hist_avg_ms = prof["rs_histogram"][1] / max(prof["rs_histogram"][0], 1)
+
+    # ---- e2e through the public API with host buffers ---------------------------
+    sorter = DeviceRadixSort()
+    sorter.create(None)
+    api_stream = Stream(stream)
+    e2e_steps = max(2, min(5, args.steps))
+    cmd = CommandList()
+    sorter.SortPairs(cmd, d_temp, d_keys, d_keys_out, d_vals, d_vals_out, n)  # warm the path
+    api_stream << cmd.commit() << synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        d_keys.copy_(h_keys, non_blocking=True)
+        d_vals.copy_(h_vals, non_blocking=True)
+        cmd = CommandList()
+        sorter.SortPairs(cmd, d_temp, d_keys, d_keys_out, d_vals, d_vals_out, n)
+        api_stream << cmd.commit()
+        h_keys_out.copy_(d_keys_out, non_blocking=True)
+        h_vals_out.copy_(d_vals_out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    e2e_value = world * n / (e2e_ms * 1e-3) / 1e9
+    assert np.array_equal(h_vals_out[:1000].numpy(), d_vals_out[:1000].cpu().numpy())
+
+    # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------
+    cpu = None
+    if rank == 0 and world == 1:
+        cores = os.cpu_count() or 1
+        sample = 1 << 24
+        ks, vs = keys_np[:sample].copy(), np.arange(sample, dtype=np.uint32)
+        oracle.radix_sort(ks, vs, threads=cores)
+        reps, t0 = 3, time.perf_counter()
+        for _ in range(reps):
+            oracle.radix_sort(ks, vs, threads=cores)
+        sec = (time.perf_counter() - t0) / reps
+        cpu = {"value": sample / sec / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{sample} of the 2^28 pairs, LSD radix sort (oracle/), {reps} reps"}
+
+    extras = {}
+    if not args.no_extras:
+        del h_keys_out, h_vals_out
+        extras = run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u32", "data": "synthetic (PCG32 seeded, uniform u32 keys, iota values)",
+            "config": {"workload": "DeviceRadixSort::SortPairs, n=2^28 u32 keys + u32 values per GPU (BASELINE config 3)",
+                       "n_per_gpu": n, "parallelism": f"independent shards x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs 2 GiB per step > 126 MB L2 (no flush needed)",
+                       "algorithmic_bytes_per_pair": 68},
+            "roofline": {"bound": "hbm", "kernel": "rs_onesweep_kernel (one 8-bit pass)",
+                         "achieved": os_achieved, "peak": peak, "unit": "GB/s", "frac": os_achieved / peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                         "traffic": None, "avg_launch_ms": os_avg_ms, "bytes_per_launch": os_bytes,
+                         "whole_sort_frac": (68 * n / (ms * 1e-3) / 1e9) / peak},
+            "kernels": {k: {"launches": c, "total_ms": t} for k, (c, t) in prof.items()},
+            "histogram_avg_ms": hist_avg_ms,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 8 * n,
+                    "ms_per_step": e2e_ms, "api": "DeviceRadixSort.SortPairs via CommandList/Stream",
+                    "steps": e2e_steps},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "extras": extras,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier):
+    """Scan (config 2), reduce (config 1) and segment reduce (config 4), each
+    timed with CUDA events; GB/s from algorithmic bytes."""
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    out = {}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def timeit(fn, iters, flush_l2=False):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(iters):
+            if flush_l2:
+                flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b)
+        return max_over_ranks(tot / iters)
+
+    # scan: 2^28 u32 exclusive, 2^28 f32 inclusive
+    n = 1 << 28
+    x = torch.from_numpy(G.u32_below(n, 16, seed=1, stream=5).view(np.int32)).to(dev)
+    y = torch.empty_like(x)
+    tb = lib.lcpp_scan_temp_bytes(L.U32, n)
+    t = torch.empty(tb, dtype=torch.uint8, device=dev)
+    ms = timeit(lambda: L.check(lib.lcpp_scan(0, L.U32, x.data_ptr(), y.data_ptr(), n, t.data_ptr(), tb, sh)), 20)
+    out["scan_exclusive_u32_2p28"] = {"ms": ms, "GB/s": 8 * n / ms / 1e6, "frac": 8 * n / ms / 1e6 / peak}
+    xf = torch.from_numpy(G.f32_normal(n, seed=1, stream=5)).to(dev)
+    ms = timeit(lambda: L.check(lib.lcpp_scan(1, L.F32, xf.data_ptr(), y.data_ptr(), n, t.data_ptr(), tb, sh)), 20)
+    out["scan_inclusive_f32_2p28"] = {"ms": ms, "GB/s": 8 * n / ms / 1e6, "frac": 8 * n / ms / 1e6 / peak}
+    del xf, y, t
+
+    # reduce: 2^24 int32 (L2 flushed between iterations) and 2^28 int32
+    for logn in (24, 28):
+        n = 1 << logn
+        xr = x[:n] if logn == 28 else torch.from_numpy(G.i32_range(n, -1000, 1000, seed=1, stream=3)).to(dev)
+        o = torch.empty(1, dtype=torch.int32, device=dev)
+        tb = lib.lcpp_reduce_temp_bytes(L.I32, n)
+        t = torch.empty(tb, dtype=torch.uint8, device=dev)
+        ms = timeit(lambda: L.check(lib.lcpp_reduce(0, L.I32, xr.data_ptr(), o.data_ptr(), n, t.data_ptr(), tb, sh)),
+                    30, flush_l2=True)
+        out[f"reduce_sum_i32_2p{logn}"] = {"ms": ms, "GB/s": 4 * n / ms / 1e6, "frac": 4 * n / ms / 1e6 / peak}
+    del x
+
+    # segment reduce: 2^27 f32, 2^20 lognormal segments
+    N, S = 1 << 27, 1 << 20
+    off = G.lognormal_offsets(S, N, seed=1, stream=9)
+    xs = torch.from_numpy(G.f32_unit(N, seed=1, stream=10)).to(dev)
+    b = torch.from_numpy(off[:-1].view(np.int32).copy()).to(dev)
+    e = torch.from_numpy(off[1:].view(np.int32).copy()).to(dev)
+    o = torch.empty(S, dtype=torch.float32, device=dev)
+    tb = lib.lcpp_segment_reduce_temp_bytes(L.F32, N, S)
+    t = torch.empty(tb, dtype=torch.uint8, device=dev)
+    ms = timeit(lambda: L.check(lib.lcpp_segment_reduce(0, L.F32, xs.data_ptr(), o.data_ptr(), S, b.data_ptr(),
+                                                        e.data_ptr(), t.data_ptr(), tb, sh)), 20)
+    byts = 4 * N + 4 * (S + 1) + 4 * S + 4 * S
+    out["segment_sum_f32_2p27_2p20"] = {"ms": ms, "GB/s": byts / ms / 1e6, "frac": byts / ms / 1e6 / peak}
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

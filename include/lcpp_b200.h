@@ -1,0 +1,181 @@
+/*
+ * lcpp_b200.h — C ABI of liblcpp_b200.so, the B200 (sm_100a) implementation of
+ * LCPP's device-level primitives (DeviceReduce, DeviceScan, DeviceRadixSort,
+ * DeviceSegmentReduce).
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers unless the name says host.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Every call is asynchronous on `stream`, allocates no device memory and
+ *     takes its scratch space from the caller's `temp` buffer, whose size is
+ *     given by the matching *_temp_bytes() function (CUB-style two-phase use,
+ *     as in the reference's GetTempStorageBytes).  `temp` must be 256-byte
+ *     aligned (cudaMalloc memory always is).
+ *   - Return value: LCPP_OK or a negative lcpp_status.  Launch-time errors are
+ *     returned directly; device-side errors (a look-back wait that gave up)
+ *     are latched in a per-device error word read by lcpp_last_device_error().
+ *   - Calls are reentrant: distinct calls on distinct streams with distinct
+ *     temp buffers are independent.
+ *
+ * Reference interfaces replaced (paths inside Ligo04/lc_parallel_primitive):
+ *   DeviceReduce        src/lcpp/device/device_reduce.h:84-91,131-185
+ *   DeviceScan          src/lcpp/device/device_scan.h:75-89,114-204
+ *   DeviceRadixSort     src/lcpp/device/device_radix_sort.h:83-184
+ *   DeviceSegmentReduce src/lcpp/device/device_segment_reduce.h:71-194
+ * The C++ class templates of those files are kept, with the same names and
+ * signatures, in include/lcpp/ and forward to the functions below.
+ */
+#ifndef LCPP_B200_H
+#define LCPP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int lcpp_status;
+
+enum {
+    LCPP_OK                   = 0,
+    LCPP_ERR_INVALID_ARG      = -1, /* bad dtype/op, null pointer, n too large  */
+    LCPP_ERR_TEMP_TOO_SMALL   = -2, /* temp_bytes < *_temp_bytes()               */
+    LCPP_ERR_CUDA             = -3, /* a CUDA runtime call or launch failed      */
+    LCPP_ERR_LOOKBACK_TIMEOUT = -4, /* a look-back wait hit its iteration cap    */
+    LCPP_ERR_NCCL             = -5, /* an NCCL call failed (multi-GPU entries)   */
+    LCPP_ERR_UNSUPPORTED      = -6  /* valid request this build does not serve   */
+};
+
+/* Element types.  The reference's NumericT (common/type_trait.h:11-14) admits
+ * every integral and floating type; this ABI serves the 4- and 8-byte ones. */
+typedef enum {
+    LCPP_I32 = 0,
+    LCPP_U32 = 1,
+    LCPP_F32 = 2,
+    LCPP_I64 = 3,
+    LCPP_U64 = 4,
+    LCPP_F64 = 5,
+    LCPP_NONE = 15 /* "no values" for SortKeys */
+} lcpp_dtype;
+
+/* Reduction operators: SumOp / MinOp / MaxOp of common/thread_operators.h. */
+typedef enum { LCPP_OP_SUM = 0, LCPP_OP_MIN = 1, LCPP_OP_MAX = 2 } lcpp_op;
+
+typedef enum { LCPP_SCAN_EXCLUSIVE = 0, LCPP_SCAN_INCLUSIVE = 1 } lcpp_scan_kind;
+
+const char* lcpp_status_string(lcpp_status s);
+size_t      lcpp_dtype_size(int dtype);
+
+/* ---- DeviceReduce ------------------------------------------------------
+ * out[0] = init (+) reduce(in[0..n)), init = 0 / +max / lowest for
+ * Sum / Min / Max.  Replaces DeviceReduce::Sum/Min/Max
+ * (device_reduce.h:169-185) and GetTempStorageBytes (device_reduce.h:84-91).
+ * Max starts from numeric_limits<T>::lowest() (the reference's min() at
+ * device_reduce.h:184 is wrong for negative floats; ints are identical).
+ * dtype: any of I32 U32 F32 I64 U64 F64.  Integer sums wrap (mod 2^bits). */
+size_t      lcpp_reduce_temp_bytes(int dtype, uint64_t n);
+lcpp_status lcpp_reduce(int op, int dtype, const void* in, void* out, uint64_t n,
+                        void* temp, size_t temp_bytes, void* stream);
+
+/* ---- DeviceScan ---------------------------------------------------------
+ * Exclusive: out[i] = sum(in[0..i)), out[0] = 0.  Inclusive: sum(in[0..i]).
+ * Replaces DeviceScan::ExclusiveSum/InclusiveSum (device_scan.h:180-204) and
+ * GetTempStorageBytes (device_scan.h:75-89).  Single-pass decoupled
+ * look-back.  dtype: I32 U32 F32 (the reference's Type4Byte).  In-place
+ * (in == out) is allowed. */
+size_t      lcpp_scan_temp_bytes(int dtype, uint64_t n);
+lcpp_status lcpp_scan(int kind, int dtype, const void* in, void* out, uint64_t n,
+                      void* temp, size_t temp_bytes, void* stream);
+/* Same, with every output offset by the device scalar *carry_in (same dtype);
+ * carry_in == NULL means 0.  Used by the sharded multi-GPU scan. */
+lcpp_status lcpp_scan_carry(int kind, int dtype, const void* in, void* out, uint64_t n,
+                            const void* carry_in, void* temp, size_t temp_bytes,
+                            void* stream);
+
+/* ---- DeviceRadixSort ----------------------------------------------------
+ * Stable LSD radix sort (8-bit digits, onesweep) of keys[begin_bit,end_bit),
+ * values travelling with their keys.  keys_in/values_in are not modified.
+ * Replaces DeviceRadixSort::SortKeys/SortPairs(+Descending)
+ * (device_radix_sort.h:129-184) and Get*TempStorageBytes
+ * (device_radix_sort.h:83-122).
+ * key_dtype: I32 U32 F32 I64 U64 F64.  value_dtype: LCPP_NONE (keys only) or
+ * any 4- or 8-byte dtype (values are moved as raw bits).  Floats order by
+ * value with -0.0 == +0.0 (radix_rank_sort_operations.h:30-43); NaNs order by
+ * bit pattern.  n < 2^32.  begin_bit/end_bit as in CUB (0 / 8*sizeof(K) for
+ * a full sort); pass end_bit <= 0 for "all bits". */
+size_t      lcpp_radix_sort_temp_bytes(int key_dtype, int value_dtype, uint64_t n);
+lcpp_status lcpp_radix_sort(int key_dtype, int value_dtype, int descending,
+                            const void* keys_in, void* keys_out,
+                            const void* values_in, void* values_out, uint64_t n,
+                            int begin_bit, int end_bit,
+                            void* temp, size_t temp_bytes, void* stream);
+
+/* ---- DeviceSegmentReduce ------------------------------------------------
+ * out[s] = init (+) reduce(in[begin[s]..end[s])); empty segment -> init.
+ * Replaces DeviceSegmentReduce::Sum/Min/Max with begin/end offset views
+ * (device_segment_reduce.h:125-194; Max's init is lowest(), :186-194).
+ * dtype: any of I32 U32 F32 I64 U64 F64.  Offsets are uint32 (the
+ * reference's BufferView<uint>); a CSR offsets[S+1] array is passed as
+ * begin = offsets, end = offsets + 1. */
+size_t      lcpp_segment_reduce_temp_bytes(int dtype, uint64_t num_items,
+                                           uint64_t num_segments);
+lcpp_status lcpp_segment_reduce(int op, int dtype, const void* in, void* out,
+                                uint64_t num_segments, const uint32_t* begin_offsets,
+                                const uint32_t* end_offsets,
+                                void* temp, size_t temp_bytes, void* stream);
+/* Fixed-size segments: segment s is in[s*segment_size .. (s+1)*segment_size).
+ * Replaces the segment_size overloads (device_segment_reduce.h:109-123,
+ * 137-170).  Needs no temp. */
+lcpp_status lcpp_segment_reduce_fixed(int op, int dtype, const void* in, void* out,
+                                      uint64_t num_segments, uint64_t segment_size,
+                                      void* stream);
+
+/* ---- Device error word --------------------------------------------------
+ * Synchronizes `stream`, returns the first device-side error latched since
+ * the last call on the current device (LCPP_OK if none) and clears it.  The
+ * reference has no device-side error reporting (runtime/core.h:57-66). */
+lcpp_status lcpp_last_device_error(void* stream);
+
+/* ---- Look-back unit hooks ----------------------------------------------
+ * Run the scan's decoupled look-back alone, one tile per CTA, with tile t
+ * contributing aggregates[t]: exclusive_out[t] = sum(aggregates[0..t)),
+ * inclusive_out[t] = exclusive_out[t] + aggregates[t].  Mirrors the
+ * reference's stand-alone TilePrefixCallbackOp test
+ * (tests/decoupled_look_back.cpp:57-180).  temp: lcpp_lookback_temp_bytes. */
+size_t      lcpp_lookback_temp_bytes(uint64_t num_tiles);
+lcpp_status lcpp_lookback_tiles(const uint32_t* aggregates, uint32_t* exclusive_out,
+                                uint32_t* inclusive_out, uint64_t num_tiles,
+                                void* temp, size_t temp_bytes, void* stream);
+/* Caps every look-back wait at `iterations` polls (0 restores the default,
+ * about one second) on the current device. */
+lcpp_status lcpp_set_spin_limit(uint32_t iterations);
+/* One warp runs the look-back of tile `tile` against the caller's descriptor
+ * array (num_tiles 64-bit words, status in the high half: 0 = not yet
+ * published, 1 = partial, 2 = inclusive) and writes the exclusive prefix to
+ * *exclusive_out.  A descriptor that is never published makes the wait run
+ * out: the kernel returns, *exclusive_out is unspecified and
+ * lcpp_last_device_error() reports LCPP_ERR_LOOKBACK_TIMEOUT. */
+lcpp_status lcpp_lookback_probe(const uint64_t* descriptors, uint64_t tile,
+                                uint32_t* exclusive_out, void* stream);
+
+/* ---- Per-kernel timing ---------------------------------------------------
+ * lcpp_profile_enable(1) makes every launch site of this library bracket its
+ * kernel with CUDA events on the launching stream (0 turns it off); both
+ * calls reset the totals.  lcpp_profile_read() waits for the recorded events
+ * and returns, for one kernel kind ("reduce", "scan", "rs_memset",
+ * "rs_histogram", "rs_bins_scan", "rs_onesweep", "seg_warp", "seg_block"),
+ * the number of timed launches and their summed duration in ms. */
+lcpp_status lcpp_profile_enable(int on);
+lcpp_status lcpp_profile_read(const char* kernel, uint64_t* launches, double* total_ms);
+
+/* ---- Library info ------------------------------------------------------ */
+/* Number of kernels this library launched from the calling process (all
+ * devices, all streams) since load; for launch accounting in benchmarks. */
+uint64_t    lcpp_kernel_launch_count(void);
+const char* lcpp_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LCPP_B200_H */

@@ -1,0 +1,509 @@
+// DeviceRadixSort for sm_100a: onesweep LSD radix sort (Adinets & Merrill
+// 2022), the algorithm of the reference's onesweep_radix_sort
+// (src/lcpp/device/device_radix_sort.h:187-378) with its histogram agent
+// (src/lcpp/agent/agent_radix_sort_histogram.h:45-198), bins exclusive sum
+// (src/lcpp/device/details/radix_sort.h:82-123), onesweep pass agent
+// (src/lcpp/agent/agent_radix_sort_onesweep.h:43-500) and match-based block
+// rank (src/lcpp/block/block_radix_rank.h:66-336).  Key bit ordering follows
+// Traits::TwiddleIn (src/lcpp/common/util_type.h:89-176) and
+// ProcessFloatMinusZero (src/lcpp/agent/radix_rank_sort_operations.h:30-43).
+//
+// B200 design:
+//  * One upfront histogram kernel reads every key once and counts the digits
+//    of all passes (grid = SMs x 4, warp-uniform fast path for skewed keys),
+//    then one tiny kernel turns the counts into per-pass digit starts.
+//  * One onesweep kernel per 8-bit pass: 512 threads x 16 keys (8 for 64-bit
+//    keys) per tile, tile ids from an atomic ticket, warp-striped coalesced
+//    loads, stable in-warp ranking with __match_any_sync + per-warp shared
+//    counters, per-digit decoupled look-back over one 32-bit word per
+//    (tile, digit) {flags:2 | count:30} (64-bit words when n >= 2^30), then
+//    keys and values are placed in shared memory in digit order and written
+//    out with consecutive threads on consecutive addresses.
+//  * All look-back buffers of a sort are zeroed by one memset; no per-pass
+//    reset kernels (the reference resets 1 KiB per tile every pass).
+//  * Sizes are 64-bit in the ABI; no 2^28 "portions" (the reference's portion
+//    hand-off at agent_radix_sort_onesweep.h:322 is not reproduced).
+//  * Bounded look-back waits: after g_spin_limit polls a tile latches
+//    LCPP_ERR_LOOKBACK_TIMEOUT and proceeds (no trap, no hang).
+#include "common.cuh"
+#include <type_traits>
+
+namespace lcpp {
+
+constexpr int RS_BITS = 8;
+constexpr int RS_DIGITS = 1 << RS_BITS;
+constexpr int RS_THREADS = 512;
+constexpr int RS_WARPS = RS_THREADS / 32;
+constexpr int RS_MAX_PASSES = 8;
+constexpr int HIST_THREADS = 512;
+constexpr int HIST_CTAS_PER_SM = 2;
+
+template <typename KB> struct RsItems;
+template <> struct RsItems<uint32_t> { static constexpr int value = 16; };
+template <> struct RsItems<uint64_t> { static constexpr int value = 8; };
+
+struct NoValue {};
+
+// Map key bits to an unsigned order-preserving image (ascending), or its
+// complement for descending.  KIND: 0 unsigned, 1 signed, 2 floating point.
+template <typename KB, int KIND, bool DESC>
+__device__ __forceinline__ KB ordered_bits(KB k) {
+    constexpr KB HIGH = KB(1) << (sizeof(KB) * 8 - 1);
+    KB o;
+    if (KIND == 0) {
+        o = k;
+    } else if (KIND == 1) {
+        o = k ^ HIGH;
+    } else {
+        o = (k & HIGH) ? KB(~k) : KB(k ^ HIGH);
+        if (o == KB(~HIGH)) o = HIGH;  // -0.0 sorts as +0.0
+    }
+    return DESC ? KB(~o) : o;
+}
+
+template <typename KB, int KIND, bool DESC>
+__device__ __forceinline__ uint32_t digit_of(KB k, uint32_t shift, uint32_t mask) {
+    return (uint32_t)(ordered_bits<KB, KIND, DESC>(k) >> shift) & mask;
+}
+
+// ---------------------------------------------------------------------------
+// Histogram of all passes' digits.  bins[p*256 + d] += count.
+// ---------------------------------------------------------------------------
+template <typename KB, int KIND, bool DESC>
+__global__ void __launch_bounds__(HIST_THREADS)
+rs_histogram_kernel(const KB* __restrict__ keys, uint64_t n, uint32_t* __restrict__ bins,
+                    uint32_t begin_bit, uint32_t end_bit, uint32_t passes) {
+    __shared__ uint32_t sh[RS_MAX_PASSES][RS_DIGITS];
+    for (int i = threadIdx.x; i < RS_MAX_PASSES * RS_DIGITS; i += blockDim.x) (&sh[0][0])[i] = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+
+    auto count_key = [&](KB k, bool valid) {
+        const KB o = ordered_bits<KB, KIND, DESC>(k);
+#pragma unroll
+        for (uint32_t p = 0; p < RS_MAX_PASSES; ++p) {
+            if (p >= passes) break;
+            const uint32_t shift = begin_bit + p * RS_BITS;
+            const uint32_t nb = min((uint32_t)RS_BITS, end_bit - shift);
+            const uint32_t d = (uint32_t)(o >> shift) & ((1u << nb) - 1u);
+            const uint32_t d0 = __shfl_sync(0xffffffffu, d, 0);
+            const bool all_valid = __all_sync(0xffffffffu, valid);
+            if (all_valid && __all_sync(0xffffffffu, d == d0)) {
+                if (lane == 0) atomicAdd(&sh[p][d0], 32u);
+            } else if (valid) {
+                atomicAdd(&sh[p][d], 1u);
+            }
+        }
+    };
+
+    constexpr int VEC = 16 / sizeof(KB);
+    const bool aligned = (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
+    const uint64_t nvec = aligned ? n / VEC : 0;
+    const uint4* vk = reinterpret_cast<const uint4*>(keys);
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    // Whole warps iterate together so the warp-uniform fast path stays legal.
+    const uint64_t nvec_pad = (nvec + 31) / 32 * 32;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec_pad; i += stride) {
+        const bool valid = i < nvec;
+        uint4 q = valid ? ld_stream(vk + i) : make_uint4(0, 0, 0, 0);
+        const KB* e = reinterpret_cast<const KB*>(&q);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) count_key(e[v], valid);
+    }
+    // Scalar tail (all keys when the base is not 16-byte aligned).
+    const uint64_t t0 = nvec * VEC;
+    const uint64_t ntail_pad = (n - t0 + 31) / 32 * 32;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ntail_pad; i += stride) {
+        const bool valid = t0 + i < n;
+        count_key(valid ? keys[t0 + i] : KB(0), valid);
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < passes * RS_DIGITS; i += blockDim.x) {
+        const uint32_t c = (&sh[0][0])[i];
+        if (c) atomicAdd(bins + i, c);
+    }
+}
+
+// In-place exclusive scan of each pass's 256 counts (one CTA per pass).
+__global__ void __launch_bounds__(RS_DIGITS) rs_bins_scan_kernel(uint32_t* bins) {
+    __shared__ uint32_t s_w[RS_DIGITS / 32];
+    uint32_t* b = bins + blockIdx.x * RS_DIGITS;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t c = b[threadIdx.x];
+    uint32_t incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_w[warp] = incl;
+    __syncthreads();
+    uint32_t wpre = 0;
+    for (int w = 0; w < warp; ++w) wpre += s_w[w];
+    b[threadIdx.x] = wpre + incl - c;
+}
+
+// ---------------------------------------------------------------------------
+// Look-back words: {INCLUSIVE | PARTIAL | count} in 32 or 64 bits.
+// ---------------------------------------------------------------------------
+template <typename W> struct LbFlags;
+template <> struct LbFlags<uint32_t> {
+    static constexpr uint32_t PART = 1u << 30, INCL = 1u << 31, MASK = PART - 1;
+};
+template <> struct LbFlags<uint64_t> {
+    static constexpr uint64_t PART = 1ull << 62, INCL = 1ull << 63, MASK = PART - 1;
+};
+__device__ __forceinline__ uint32_t lb_load(const uint32_t* p) { return ld_relaxed_u32(p); }
+__device__ __forceinline__ uint64_t lb_load(const uint64_t* p) { return ld_relaxed_u64(p); }
+__device__ __forceinline__ void lb_store(uint32_t* p, uint32_t v) { st_relaxed_u32(p, v); }
+__device__ __forceinline__ void lb_store(uint64_t* p, uint64_t v) { st_relaxed_u64(p, v); }
+
+struct RsPass {
+    const void* keys_in;
+    void* keys_out;
+    const void* vals_in;
+    void* vals_out;
+    uint64_t n;
+    uint32_t shift;
+    uint32_t mask;
+    const uint32_t* bins;   // 256 global digit starts of this pass
+    void* lookback;         // tiles x 256 words, zeroed
+    uint32_t* ticket;       // zeroed
+};
+
+template <typename KB, typename VB>
+constexpr size_t rs_smem_bytes() {
+    constexpr int TILE = RS_THREADS * RsItems<KB>::value;
+    return (size_t)TILE * sizeof(KB) +
+           (std::is_same<VB, NoValue>::value ? 0 : (size_t)TILE * sizeof(VB)) +
+           (size_t)RS_WARPS * RS_DIGITS * 4 + RS_DIGITS * 4 * 2 + 64;
+}
+
+template <typename KB, typename VB, typename W, int KIND, bool DESC>
+__global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
+    constexpr int ITEMS = RsItems<KB>::value;
+    constexpr int TILE = RS_THREADS * ITEMS;
+    constexpr bool HAS_V = !std::is_same<VB, NoValue>::value;
+    using F = LbFlags<W>;
+
+    extern __shared__ __align__(16) unsigned char smem[];
+    KB* s_keys = reinterpret_cast<KB*>(smem);
+    unsigned char* p = smem + (size_t)TILE * sizeof(KB);
+    VB* s_vals = reinterpret_cast<VB*>(p);
+    if constexpr (HAS_V) p += (size_t)TILE * sizeof(VB);
+    uint32_t* s_wc = reinterpret_cast<uint32_t*>(p);          // [RS_WARPS][256]
+    uint32_t* s_gbase = s_wc + RS_WARPS * RS_DIGITS;         // [256]
+    uint32_t* s_misc = s_gbase + RS_DIGITS;                  // [0] tile id, [1..8] warp sums
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) s_misc[0] = atomicAdd(a.ticket, 1u);
+    for (int i = tid; i < RS_WARPS * RS_DIGITS; i += RS_THREADS) s_wc[i] = 0;
+    __syncthreads();
+    const uint64_t tile = s_misc[0];
+    const uint64_t tile_base = tile * TILE;
+    const uint64_t rem = a.n - tile_base;
+    const uint32_t num_valid = rem < (uint64_t)TILE ? (uint32_t)rem : (uint32_t)TILE;
+
+    const KB* kin = reinterpret_cast<const KB*>(a.keys_in);
+    const uint32_t wbase = (uint32_t)warp * (ITEMS * 32);
+
+    // ---- load (warp-striped) -------------------------------------------------
+    KB key[ITEMS];
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+        const uint32_t li = wbase + i * 32 + lane;
+        key[i] = li < num_valid ? ldcs(kin + tile_base + li) : KB(0);
+    }
+
+    // ---- stable in-warp rank ---------------------------------------------------
+    uint32_t* wc = s_wc + warp * RS_DIGITS;
+    const uint32_t lt = lanemask_lt();
+    uint32_t rank[ITEMS];  // (rank within warp & digit) | digit << 16
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+        const uint32_t li = wbase + i * 32 + lane;
+        const uint32_t d = li < num_valid ? digit_of<KB, KIND, DESC>(key[i], a.shift, a.mask) : (RS_DIGITS - 1);
+        const uint32_t peers = __match_any_sync(0xffffffffu, d);
+        const int leader = 31 - __clz(peers);
+        uint32_t old = 0;
+        if (lane == leader) old = atomicAdd(wc + d, (uint32_t)__popc(peers));
+        old = __shfl_sync(0xffffffffu, old, leader);
+        rank[i] = (old + __popc(peers & lt)) | (d << 16);
+    }
+    __syncthreads();
+
+    // ---- per-digit tile counts, partial publish, tile-local digit offsets ---
+    W* lb = reinterpret_cast<W*>(a.lookback);
+    uint32_t total = 0;
+    if (tid < RS_DIGITS) {
+#pragma unroll
+        for (int w = 0; w < RS_WARPS; ++w) total += s_wc[w * RS_DIGITS + tid];
+        if (tile == 0)
+            lb_store(lb + tid, F::INCL | (W)(a.bins[tid] + total));
+        else
+            lb_store(lb + tile * RS_DIGITS + tid, F::PART | (W)total);
+    }
+    // exclusive scan of the 256 totals (threads 0..255 = warps 0..7)
+    uint32_t incl = total;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31 && warp < RS_DIGITS / 32) s_misc[1 + warp] = incl;
+    __syncthreads();
+    uint32_t off = 0;
+    if (tid < RS_DIGITS) {
+        for (int w = 0; w < warp; ++w) off += s_misc[1 + w];
+        off += incl - total;
+        uint32_t run = off;
+#pragma unroll
+        for (int w = 0; w < RS_WARPS; ++w) {
+            const uint32_t c = s_wc[w * RS_DIGITS + tid];
+            s_wc[w * RS_DIGITS + tid] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+
+    // ---- keys into shared memory in digit order -------------------------------
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+        const uint32_t d = rank[i] >> 16;
+        s_keys[wc[d] + (rank[i] & 0xffffu)] = key[i];
+    }
+
+    // ---- per-digit look-back (threads 0..255) ---------------------------------
+    if (tid < RS_DIGITS) {
+        W excl;
+        if (tile == 0) {
+            excl = a.bins[tid];
+        } else {
+            W acc = 0;
+            uint64_t pt = tile - 1;
+            uint32_t spins = 0;
+            const uint32_t limit = g_spin_limit;
+            while (true) {
+                W w = lb_load(lb + pt * RS_DIGITS + tid);
+                while ((w & (F::PART | F::INCL)) == 0) {
+                    if (++spins > limit) {
+                        set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
+                        break;
+                    }
+                    if (spins > 4) __nanosleep(spins < 64 ? 32 : 256);
+                    w = lb_load(lb + pt * RS_DIGITS + tid);
+                }
+                acc += w & F::MASK;
+                if ((w & F::INCL) || pt == 0 || spins > limit) break;
+                --pt;
+            }
+            excl = acc;
+            lb_store(lb + tile * RS_DIGITS + tid, F::INCL | (excl + total));
+        }
+        s_gbase[tid] = (uint32_t)excl - off;
+    }
+
+    // ---- values into shared memory in digit order -----------------------------
+    if constexpr (HAS_V) {
+        const VB* vin = reinterpret_cast<const VB*>(a.vals_in);
+        VB val[ITEMS];
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {
+            const uint32_t li = wbase + i * 32 + lane;
+            if (li < num_valid) val[i] = ldcs(vin + tile_base + li);
+        }
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {
+            const uint32_t li = wbase + i * 32 + lane;
+            const uint32_t d = rank[i] >> 16;
+            if (li < num_valid) s_vals[wc[d] + (rank[i] & 0xffffu)] = val[i];
+        }
+    }
+    __syncthreads();
+
+    // ---- coalesced write-out ----------------------------------------------------
+    KB* kout = reinterpret_cast<KB*>(a.keys_out);
+    VB* vout = reinterpret_cast<VB*>(a.vals_out);
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+        const uint32_t idx = i * RS_THREADS + tid;
+        if (idx < num_valid) {
+            const KB k = s_keys[idx];
+            const uint32_t d = digit_of<KB, KIND, DESC>(k, a.shift, a.mask);
+            const uint32_t g = s_gbase[d] + idx;
+            stcs(kout + g, k);
+            if constexpr (HAS_V) stcs(vout + g, s_vals[idx]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+struct RsLayout {
+    uint32_t passes;
+    uint64_t tiles;
+    size_t lb_word;
+    size_t bins_off, ticket_off, lb_off, keys_off, vals_off, total, zero_bytes;
+};
+
+static RsLayout rs_layout(size_t ksize, size_t vsize, uint64_t n, uint32_t passes) {
+    RsLayout L{};
+    const int items = ksize == 4 ? RsItems<uint32_t>::value : RsItems<uint64_t>::value;
+    L.passes = passes;
+    L.tiles = ceil_div(n ? n : 1, (uint64_t)RS_THREADS * items);
+    L.lb_word = n < (1ull << 30) ? 4 : 8;
+    L.bins_off = 0;
+    L.ticket_off = align_up(RS_MAX_PASSES * RS_DIGITS * 4, 256);
+    L.lb_off = L.ticket_off + 256;
+    L.keys_off = align_up(L.lb_off + (size_t)passes * L.tiles * RS_DIGITS * L.lb_word, 256);
+    L.zero_bytes = L.lb_off + (size_t)passes * L.tiles * RS_DIGITS * L.lb_word;
+    const bool alt = passes > 1;
+    L.vals_off = align_up(L.keys_off + (alt ? n * ksize : 0), 256);
+    L.total = align_up(L.vals_off + (alt ? n * vsize : 0), 256);
+    return L;
+}
+
+static int key_kind(int dtype) {
+    switch (dtype) {
+        case LCPP_U32: case LCPP_U64: return 0;
+        case LCPP_I32: case LCPP_I64: return 1;
+        case LCPP_F32: case LCPP_F64: return 2;
+        default: return -1;
+    }
+}
+
+template <typename KB, typename VB, typename W, int KIND, bool DESC>
+static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out, const void* vals_in,
+                          void* vals_out, uint64_t n, uint32_t begin_bit, uint32_t end_bit, char* temp,
+                          cudaStream_t s) {
+    uint32_t* bins = (uint32_t*)(temp + L.bins_off);
+    uint32_t* tickets = (uint32_t*)(temp + L.ticket_off);
+    char* lb = temp + L.lb_off;
+    {
+        ProfScope ps("rs_memset", s);
+        if (cudaMemsetAsync(temp, 0, L.zero_bytes, s) != cudaSuccess) return LCPP_ERR_CUDA;
+    }
+
+    const DeviceInfo di = device_info();
+    {
+        const uint64_t per_cta = (uint64_t)HIST_THREADS * (16 / sizeof(KB)) * 4;
+        uint64_t g = ceil_div(n, per_cta);
+        const uint64_t cap = (uint64_t)di.sms * HIST_CTAS_PER_SM;
+        if (g > cap) g = cap;
+        if (g == 0) g = 1;
+        { ProfScope ps("rs_histogram", s);
+        rs_histogram_kernel<KB, KIND, DESC><<<(unsigned)g, HIST_THREADS, 0, s>>>(
+            (const KB*)keys_in, n, bins, begin_bit, end_bit, L.passes); }
+        { ProfScope ps("rs_bins_scan", s);
+        rs_bins_scan_kernel<<<L.passes, RS_DIGITS, 0, s>>>(bins); }
+        count_launch(2);
+    }
+    constexpr size_t smem = rs_smem_bytes<KB, VB>();
+    auto kern = rs_onesweep_kernel<KB, VB, W, KIND, DESC>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return LCPP_ERR_CUDA;
+
+    const size_t ks = sizeof(KB);
+    const size_t vs = std::is_same<VB, NoValue>::value ? 0 : sizeof(VB);
+    void* kalt = temp + L.keys_off;
+    void* valt = vs ? (void*)(temp + L.vals_off) : nullptr;
+    const void* kcur = keys_in;
+    const void* vcur = vals_in;
+    for (uint32_t p = 0; p < L.passes; ++p) {
+        // The pass whose distance to the last pass is even writes keys_out.
+        const bool to_out = ((L.passes - 1 - p) & 1) == 0;
+        RsPass a;
+        a.keys_in = kcur;
+        a.vals_in = vcur;
+        a.keys_out = to_out ? keys_out : kalt;
+        a.vals_out = vs ? (to_out ? vals_out : valt) : nullptr;
+        a.n = n;
+        a.shift = begin_bit + p * RS_BITS;
+        const uint32_t nb = end_bit - a.shift < (uint32_t)RS_BITS ? end_bit - a.shift : (uint32_t)RS_BITS;
+        a.mask = (1u << nb) - 1u;
+        a.bins = bins + p * RS_DIGITS;
+        a.lookback = lb + (size_t)p * L.tiles * RS_DIGITS * L.lb_word;
+        a.ticket = tickets + p;
+        { ProfScope ps("rs_onesweep", s);
+        kern<<<(unsigned)L.tiles, RS_THREADS, smem, s>>>(a); }
+        count_launch();
+        kcur = a.keys_out;
+        vcur = a.vals_out;
+        (void)ks;
+    }
+    return check_launch();
+}
+
+template <typename KB, typename VB, int KIND>
+static lcpp_status rs_dispatch_w(const RsLayout& L, bool desc, const void* ki, void* ko, const void* vi,
+                                 void* vo, uint64_t n, uint32_t bb, uint32_t eb, char* t, cudaStream_t s) {
+    if (L.lb_word == 4)
+        return desc ? rs_run<KB, VB, uint32_t, KIND, true>(L, ki, ko, vi, vo, n, bb, eb, t, s)
+                    : rs_run<KB, VB, uint32_t, KIND, false>(L, ki, ko, vi, vo, n, bb, eb, t, s);
+    return desc ? rs_run<KB, VB, uint64_t, KIND, true>(L, ki, ko, vi, vo, n, bb, eb, t, s)
+                : rs_run<KB, VB, uint64_t, KIND, false>(L, ki, ko, vi, vo, n, bb, eb, t, s);
+}
+
+template <typename KB, typename VB>
+static lcpp_status rs_dispatch_kind(int kind, const RsLayout& L, bool desc, const void* ki, void* ko,
+                                    const void* vi, void* vo, uint64_t n, uint32_t bb, uint32_t eb,
+                                    char* t, cudaStream_t s) {
+    switch (kind) {
+        case 0: return rs_dispatch_w<KB, VB, 0>(L, desc, ki, ko, vi, vo, n, bb, eb, t, s);
+        case 1: return rs_dispatch_w<KB, VB, 1>(L, desc, ki, ko, vi, vo, n, bb, eb, t, s);
+        default: return rs_dispatch_w<KB, VB, 2>(L, desc, ki, ko, vi, vo, n, bb, eb, t, s);
+    }
+}
+
+static bool rs_bits(int key_dtype, int& begin_bit, int& end_bit, uint32_t& passes) {
+    const int kbits = (int)lcpp_dtype_size(key_dtype) * 8;
+    if (end_bit <= 0) end_bit = kbits;
+    if (begin_bit < 0 || end_bit > kbits || begin_bit >= end_bit) return false;
+    passes = (uint32_t)ceil_div((uint64_t)(end_bit - begin_bit), RS_BITS);
+    return true;
+}
+
+}  // namespace lcpp
+
+using namespace lcpp;
+
+extern "C" size_t lcpp_radix_sort_temp_bytes(int key_dtype, int value_dtype, uint64_t n) {
+    if (key_kind(key_dtype) < 0) return 0;
+    const size_t ks = lcpp_dtype_size(key_dtype);
+    const size_t vs = value_dtype == LCPP_NONE ? 0 : lcpp_dtype_size(value_dtype);
+    if (value_dtype != LCPP_NONE && vs == 0) return 0;
+    return rs_layout(ks, vs, n, (uint32_t)(ks * 8 / RS_BITS)).total;
+}
+
+extern "C" lcpp_status lcpp_radix_sort(int key_dtype, int value_dtype, int descending,
+                                       const void* keys_in, void* keys_out,
+                                       const void* values_in, void* values_out, uint64_t n,
+                                       int begin_bit, int end_bit,
+                                       void* temp, size_t temp_bytes, void* stream) {
+    const int kind = key_kind(key_dtype);
+    if (kind < 0) return LCPP_ERR_INVALID_ARG;
+    const size_t ks = lcpp_dtype_size(key_dtype);
+    const size_t vs = value_dtype == LCPP_NONE ? 0 : lcpp_dtype_size(value_dtype);
+    if (value_dtype != LCPP_NONE && vs == 0) return LCPP_ERR_INVALID_ARG;
+    if (n >= (1ull << 32)) return LCPP_ERR_INVALID_ARG;
+    uint32_t passes = 0;
+    if (!rs_bits(key_dtype, begin_bit, end_bit, passes)) return LCPP_ERR_INVALID_ARG;
+    if (n == 0) return LCPP_OK;
+    if (!keys_in || !keys_out || (vs && (!values_in || !values_out))) return LCPP_ERR_INVALID_ARG;
+    // Temp is sized for a full-width sort; fewer bits need no more.
+    if (!temp || temp_bytes < lcpp_radix_sort_temp_bytes(key_dtype, value_dtype, n)) return LCPP_ERR_TEMP_TOO_SMALL;
+    const RsLayout L = rs_layout(ks, vs, n, passes);
+    cudaStream_t s = (cudaStream_t)stream;
+    char* t = (char*)temp;
+    const bool desc = descending != 0;
+    const uint32_t bb = (uint32_t)begin_bit, eb = (uint32_t)end_bit;
+    if (ks == 4) {
+        if (vs == 0) return rs_dispatch_kind<uint32_t, NoValue>(kind, L, desc, keys_in, keys_out, nullptr, nullptr, n, bb, eb, t, s);
+        if (vs == 4) return rs_dispatch_kind<uint32_t, uint32_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
+        return rs_dispatch_kind<uint32_t, uint64_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
+    }
+    if (vs == 0) return rs_dispatch_kind<uint64_t, NoValue>(kind, L, desc, keys_in, keys_out, nullptr, nullptr, n, bb, eb, t, s);
+    if (vs == 4) return rs_dispatch_kind<uint64_t, uint32_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
+    return rs_dispatch_kind<uint64_t, uint64_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
+}

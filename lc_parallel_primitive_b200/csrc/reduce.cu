@@ -1,0 +1,146 @@
+// DeviceReduce for sm_100a: one grid-stride kernel with 128-bit streaming
+// loads and a last-CTA-done combine, so a full reduction is one launch (plus a
+// 4-byte memset of the ticket counter).
+//
+// Reference behaviour followed: DeviceReduce::Reduce / reduce_array_recursive
+// (src/lcpp/device/device_reduce.h:131-147, 396-460), AgentReduce tile
+// consumption (src/lcpp/agent/agent_reduce.h:59-157) and the single-tile
+// finalisation out = reduce_op(init, aggregate)
+// (src/lcpp/device/details/reduce.h:214-237).  The reference reduces level by
+// level (3 launches + a copy at n = 2^24); here the partials of one level are
+// combined in-kernel by the last CTA to finish, in a fixed order, so float
+// results are deterministic for a given n and GPU.
+#include "common.cuh"
+
+namespace lcpp {
+
+constexpr int REDUCE_THREADS = 512;
+constexpr int REDUCE_CTAS_PER_SM = 4;
+constexpr int REDUCE_UNROLL = 4;   // independent 16-byte loads in flight per thread
+constexpr int REDUCE_MAX_GRID = 148 * 8;
+
+template <typename Op, typename T>
+__device__ __forceinline__ T block_reduce(T v, T* s_warp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_reduce<Op>(v);
+    if (lane == 0) s_warp[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < (int)(blockDim.x >> 5) ? s_warp[lane] : Op::template identity<T>();
+        v = warp_reduce<Op>(v);
+    }
+    return v;  // valid in warp 0
+}
+
+// Accumulate the 16-byte vector `q` (VEC elements of T) into acc.
+template <typename Op, typename T, int VEC>
+__device__ __forceinline__ T fold_vec(T acc, const uint4& q) {
+    const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc = Op::template apply<T>(acc, e[i]);
+    return acc;
+}
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(REDUCE_THREADS)
+reduce_kernel(const T* __restrict__ in, uint64_t n, T* __restrict__ partials,
+              unsigned int* __restrict__ ticket, T* __restrict__ out, T init) {
+    constexpr int VEC = 16 / sizeof(T);
+    __shared__ T s_warp[REDUCE_THREADS / 32];
+    __shared__ bool s_last;
+
+    T acc = Op::template identity<T>();
+    // Scalar head up to the first 16-byte boundary, vector body, scalar tail.
+    const uint64_t mis = (reinterpret_cast<uintptr_t>(in) & 15) / sizeof(T);
+    uint64_t head = mis ? (uint64_t)(VEC - mis) : 0;
+    if (head > n) head = n;
+    const uint64_t gtid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t gstride = (uint64_t)gridDim.x * blockDim.x;
+    if (gtid < head) acc = Op::template apply<T>(acc, in[gtid]);
+
+    const uint4* vin = reinterpret_cast<const uint4*>(in + head);
+    const uint64_t nvec = (n - head) / VEC;
+    uint64_t i = gtid;
+    for (; i + (REDUCE_UNROLL - 1) * gstride < nvec; i += REDUCE_UNROLL * gstride) {
+        uint4 q[REDUCE_UNROLL];
+#pragma unroll
+        for (int u = 0; u < REDUCE_UNROLL; ++u) q[u] = ld_stream(vin + i + u * gstride);
+#pragma unroll
+        for (int u = 0; u < REDUCE_UNROLL; ++u) acc = fold_vec<Op, T, VEC>(acc, q[u]);
+    }
+    for (; i < nvec; i += gstride) acc = fold_vec<Op, T, VEC>(acc, ld_stream(vin + i));
+    const uint64_t tail0 = head + nvec * VEC;
+    if (tail0 + gtid < n) acc = Op::template apply<T>(acc, in[tail0 + gtid]);
+
+    acc = block_reduce<Op>(acc, s_warp);
+    if (threadIdx.x == 0) {
+        partials[blockIdx.x] = acc;
+        __threadfence();
+        s_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // Last CTA: combine the partials in a fixed order (thread-strided, then tree).
+    T v = Op::template identity<T>();
+    for (unsigned int b = threadIdx.x; b < gridDim.x; b += blockDim.x)
+        v = Op::template apply<T>(v, __ldcg(partials + b));
+    __syncthreads();  // s_warp reuse
+    v = block_reduce<Op>(v, s_warp);
+    if (threadIdx.x == 0) out[0] = Op::template apply<T>(init, v);
+}
+
+static unsigned int reduce_grid(uint64_t n, int elem_size) {
+    const DeviceInfo d = device_info();
+    const uint64_t per_cta = (uint64_t)REDUCE_THREADS * (16 / elem_size) * REDUCE_UNROLL;
+    uint64_t g = ceil_div(n ? n : 1, per_cta);
+    uint64_t cap = (uint64_t)d.sms * REDUCE_CTAS_PER_SM;
+    if (cap > REDUCE_MAX_GRID) cap = REDUCE_MAX_GRID;
+    if (g > cap) g = cap;
+    return (unsigned int)(g ? g : 1);
+}
+
+}  // namespace lcpp
+
+using namespace lcpp;
+
+extern "C" size_t lcpp_reduce_temp_bytes(int dtype, uint64_t n) {
+    (void)n;
+    size_t es = lcpp_dtype_size(dtype);
+    if (!es || dtype == LCPP_NONE) return 0;
+    // [ticket u32 | pad to 256][partials: one per CTA of the largest grid]
+    return 256 + align_up((size_t)REDUCE_MAX_GRID * es, 256);
+}
+
+extern "C" lcpp_status lcpp_reduce(int op, int dtype, const void* in, void* out, uint64_t n,
+                                   void* temp, size_t temp_bytes, void* stream) {
+    if (!out || (!in && n) || (op < 0 || op > 2)) return LCPP_ERR_INVALID_ARG;
+    const size_t need = lcpp_reduce_temp_bytes(dtype, n);
+    if (!need) return LCPP_ERR_INVALID_ARG;
+    if (!temp || temp_bytes < need) return LCPP_ERR_TEMP_TOO_SMALL;
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned int* ticket = (unsigned int*)temp;
+    void* partials = (char*)temp + 256;
+    if (cudaMemsetAsync(ticket, 0, sizeof(unsigned int), s) != cudaSuccess) return LCPP_ERR_CUDA;
+    return dispatch_dtype(dtype, [&](auto zero) -> lcpp_status {
+        using T = decltype(zero);
+        const unsigned int grid = reduce_grid(n, sizeof(T));
+        const T* pin = (const T*)in;
+        T* pout = (T*)out;
+        T* part = (T*)partials;
+        ProfScope ps("reduce", s);
+        switch (op) {
+            case LCPP_OP_SUM:
+                reduce_kernel<OpSum, T><<<grid, REDUCE_THREADS, 0, s>>>(pin, n, part, ticket, pout, OpSum::identity<T>());
+                break;
+            case LCPP_OP_MIN:
+                reduce_kernel<OpMin, T><<<grid, REDUCE_THREADS, 0, s>>>(pin, n, part, ticket, pout, OpMin::identity<T>());
+                break;
+            default:
+                reduce_kernel<OpMax, T><<<grid, REDUCE_THREADS, 0, s>>>(pin, n, part, ticket, pout, OpMax::identity<T>());
+                break;
+        }
+        count_launch();
+        return check_launch();
+    });
+}

@@ -1,0 +1,294 @@
+// DeviceScan for sm_100a: single-pass prefix sum with decoupled look-back
+// (Merrill & Garland 2016), the algorithm of the reference's ScanModule
+// (src/lcpp/device/details/scan.h:59-147) and TilePrefixCallbackOp
+// (src/lcpp/device/details/single_pass_scan_operator.h:138-251).
+//
+// B200 design:
+//  * 8192-item tiles (512 threads x 16 items), 128-bit streaming loads and
+//    stores; each warp owns 512 contiguous items, each thread four 16-byte
+//    vectors at a 512-byte stride, so every load/store instruction is one
+//    fully coalesced 512-byte warp access.
+//  * Thread-local scans, then shuffle scans per vector, then a 16-entry scan of
+//    warp totals: no shared-memory transpose.
+//  * Tile descriptors are single 64-bit words {status:32 | value:32} written
+//    and read with relaxed device-scope atomics, so value and status can never
+//    be seen out of step (the reference writes them separately with no fence,
+//    single_pass_scan_operator.h:81-93).
+//  * Tile ids come from an atomic ticket, so a tile only waits on tiles that
+//    already started (forward progress without co-residency assumptions).
+//  * Every wait is bounded: after g_spin_limit polls the tile latches
+//    LCPP_ERR_LOOKBACK_TIMEOUT and carries on (no trap, no hang).
+#include "common.cuh"
+
+namespace lcpp {
+
+constexpr int SCAN_THREADS = 512;
+constexpr int SCAN_WARPS = SCAN_THREADS / 32;
+constexpr int SCAN_VECS = 4;                       // 16-byte vectors per thread
+constexpr int SCAN_ITEMS = SCAN_VECS * 4;          // 16 items (4-byte types)
+constexpr int SCAN_WARP_ITEMS = 32 * SCAN_ITEMS;   // 512
+constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 8192
+constexpr size_t SCAN_HDR = 256;                   // ticket counter + padding
+
+constexpr uint64_t ST_PARTIAL = 1ull << 32;
+constexpr uint64_t ST_INCLUSIVE = 2ull << 32;
+
+template <typename T> __device__ __forceinline__ uint32_t to_bits(T v) { return __float_as_uint((float)v); }
+template <> __device__ __forceinline__ uint32_t to_bits<uint32_t>(uint32_t v) { return v; }
+template <> __device__ __forceinline__ uint32_t to_bits<int32_t>(int32_t v) { return (uint32_t)v; }
+template <typename T> __device__ __forceinline__ T from_bits(uint32_t b) { return (T)__uint_as_float(b); }
+template <> __device__ __forceinline__ uint32_t from_bits<uint32_t>(uint32_t b) { return b; }
+template <> __device__ __forceinline__ int32_t from_bits<int32_t>(uint32_t b) { return (int32_t)b; }
+
+template <typename T> __device__ __forceinline__ T add(T a, T b) { return OpSum::apply<T>(a, b); }
+
+__device__ __forceinline__ void backoff(uint32_t it) {
+    if (it > 4) __nanosleep(it < 64 ? 32 : 256);
+}
+
+// Warp-wide look-back over descriptors[0..tile): returns the sum of the
+// aggregates of all preceding tiles (same value in every lane).  Lane L
+// inspects tile (window_end - L); windows of 32 move towards tile 0 until an
+// inclusive descriptor is found.
+template <typename T>
+__device__ T lookback_warp(const uint64_t* desc, int64_t tile) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t limit = g_spin_limit;
+    T acc = T(0);
+    int64_t p = tile - 1 - lane;
+    uint32_t spins = 0;
+    while (true) {
+        uint64_t d = p >= 0 ? ld_relaxed_u64(desc + p) : ST_INCLUSIVE;
+        while (__any_sync(0xffffffffu, (d >> 32) == 0)) {
+            if (++spins > limit) {
+                if (lane == 0) set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
+                return warp_reduce<OpSum>(acc);
+            }
+            backoff(spins);
+            if ((d >> 32) == 0) d = ld_relaxed_u64(desc + p);
+        }
+        const uint32_t incl = __ballot_sync(0xffffffffu, (d >> 32) == 2);
+        T v = from_bits<T>((uint32_t)d);
+        if (incl) {
+            const int first = __ffs(incl) - 1;
+            if (lane > first) v = T(0);
+            return add(acc, warp_reduce<OpSum>(v));
+        }
+        acc = add(acc, warp_reduce<OpSum>(v));
+        p -= 32;
+    }
+}
+
+// Warp 0 of a tile: publish the tile aggregate, resolve the exclusive prefix,
+// publish the inclusive value.  Returns the exclusive prefix in every lane.
+template <typename T>
+__device__ __forceinline__ T tile_prefix(uint64_t* desc, int64_t tile, T aggregate, T carry) {
+    const int lane = threadIdx.x & 31;
+    if (tile == 0) {
+        if (lane == 0) st_relaxed_u64(desc, ST_INCLUSIVE | to_bits<T>(add(carry, aggregate)));
+        return carry;
+    }
+    if (lane == 0) st_relaxed_u64(desc + tile, ST_PARTIAL | to_bits<T>(aggregate));
+    const T excl = lookback_warp<T>(desc, tile);
+    if (lane == 0) st_relaxed_u64(desc + tile, ST_INCLUSIVE | to_bits<T>(add(excl, aggregate)));
+    return excl;
+}
+
+template <typename T, bool INCLUSIVE>
+__global__ void __launch_bounds__(SCAN_THREADS, 2)
+scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in,
+            unsigned int* ticket, uint64_t* desc) {
+    __shared__ unsigned int s_tile;
+    __shared__ T s_warp[SCAN_WARPS];
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1u);
+    __syncthreads();
+    const int64_t tile = s_tile;
+    const uint64_t tile_base = (uint64_t)tile * SCAN_TILE;
+    const uint64_t base = tile_base + (uint64_t)warp * SCAN_WARP_ITEMS + lane * 4;
+    const bool vec_ok = tile_base + SCAN_TILE <= n &&
+                        ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+
+    T x[SCAN_VECS][4];
+    if (vec_ok) {
+#pragma unroll
+        for (int j = 0; j < SCAN_VECS; ++j) {
+            const uint4 q = ld_stream(reinterpret_cast<const uint4*>(in + base + j * 128));
+            const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) x[j][k] = e[k];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < SCAN_VECS; ++j)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint64_t i = base + j * 128 + k;
+                x[j][k] = i < n ? in[i] : T(0);
+            }
+    }
+
+    // Thread-local inclusive scans, then one warp scan per vector.
+    T pre[SCAN_VECS];  // exclusive prefix of each vector within the warp
+    T carry = T(0);
+#pragma unroll
+    for (int j = 0; j < SCAN_VECS; ++j) {
+#pragma unroll
+        for (int k = 1; k < 4; ++k) x[j][k] = add(x[j][k - 1], x[j][k]);
+        T incl = x[j][3];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const T y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl = add(y, incl);
+        }
+        T excl = __shfl_up_sync(0xffffffffu, incl, 1);
+        if (lane == 0) excl = T(0);
+        pre[j] = add(carry, excl);
+        carry = add(carry, __shfl_sync(0xffffffffu, incl, 31));
+    }
+    if (lane == 0) s_warp[warp] = carry;
+    __syncthreads();
+
+    if (warp == 0) {
+        const T wt = lane < SCAN_WARPS ? s_warp[lane] : T(0);
+        T incl = wt;
+#pragma unroll
+        for (int o = 1; o < SCAN_WARPS; o <<= 1) {
+            const T y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl = add(y, incl);
+        }
+        const T aggregate = __shfl_sync(0xffffffffu, incl, SCAN_WARPS - 1);
+        const T c0 = carry_in ? *carry_in : T(0);
+        const T block_excl = tile_prefix<T>(desc, tile, aggregate, c0);
+        __syncwarp();
+        if (lane < SCAN_WARPS) {
+            T wex = __shfl_up_sync(0xffffffffu, incl, 1);
+            if (lane == 0) wex = T(0);
+            s_warp[lane] = add(block_excl, wex);
+        }
+    }
+    __syncthreads();
+    const T wbase = s_warp[warp];
+
+    if (vec_ok) {
+#pragma unroll
+        for (int j = 0; j < SCAN_VECS; ++j) {
+            const T b = add(wbase, pre[j]);
+            T r[4];
+            if (INCLUSIVE) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) r[k] = add(b, x[j][k]);
+            } else {
+                r[0] = b;
+#pragma unroll
+                for (int k = 1; k < 4; ++k) r[k] = add(b, x[j][k - 1]);
+            }
+            __stcs(reinterpret_cast<uint4*>(out + base + j * 128), *reinterpret_cast<const uint4*>(r));
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < SCAN_VECS; ++j) {
+            const T b = add(wbase, pre[j]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint64_t i = base + j * 128 + k;
+                if (i < n) out[i] = INCLUSIVE ? add(b, x[j][k]) : (k ? add(b, x[j][k - 1]) : b);
+            }
+        }
+    }
+}
+
+// ---- stand-alone look-back (unit hooks) -----------------------------------
+__global__ void lookback_tiles_kernel(const uint32_t* agg, uint32_t* excl_out, uint32_t* incl_out,
+                                      unsigned int* ticket, uint64_t* desc) {
+    __shared__ unsigned int s_tile;
+    if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1u);
+    __syncwarp();
+    const int64_t tile = s_tile;
+    const uint32_t a = agg[tile];
+    const uint32_t e = tile_prefix<uint32_t>(desc, tile, a, 0u);
+    if (threadIdx.x == 0) {
+        excl_out[tile] = e;
+        incl_out[tile] = e + a;
+    }
+}
+
+__global__ void lookback_probe_kernel(const uint64_t* desc, int64_t tile, uint32_t* excl_out) {
+    const uint32_t e = lookback_warp<uint32_t>(desc, tile);
+    if (threadIdx.x == 0) *excl_out = e;
+}
+
+}  // namespace lcpp
+
+using namespace lcpp;
+
+extern "C" size_t lcpp_scan_temp_bytes(int dtype, uint64_t n) {
+    if (dtype != LCPP_I32 && dtype != LCPP_U32 && dtype != LCPP_F32) return 0;
+    const uint64_t tiles = ceil_div(n ? n : 1, SCAN_TILE);
+    return SCAN_HDR + align_up(tiles * sizeof(uint64_t), 256);
+}
+
+extern "C" lcpp_status lcpp_scan_carry(int kind, int dtype, const void* in, void* out, uint64_t n,
+                                       const void* carry_in, void* temp, size_t temp_bytes,
+                                       void* stream) {
+    if ((kind != LCPP_SCAN_EXCLUSIVE && kind != LCPP_SCAN_INCLUSIVE) || (n && (!in || !out)))
+        return LCPP_ERR_INVALID_ARG;
+    const size_t need = lcpp_scan_temp_bytes(dtype, n);
+    if (!need) return LCPP_ERR_INVALID_ARG;
+    if (n == 0) return LCPP_OK;
+    if (!temp || temp_bytes < need) return LCPP_ERR_TEMP_TOO_SMALL;
+    const uint64_t tiles = ceil_div(n, SCAN_TILE);
+    if (tiles > 0xffffffffull) return LCPP_ERR_INVALID_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned int* ticket = (unsigned int*)temp;
+    uint64_t* desc = (uint64_t*)((char*)temp + SCAN_HDR);
+    if (cudaMemsetAsync(temp, 0, SCAN_HDR + tiles * sizeof(uint64_t), s) != cudaSuccess) return LCPP_ERR_CUDA;
+    auto go = [&](auto zero) -> lcpp_status {
+        using T = decltype(zero);
+        ProfScope ps("scan", s);
+        if (kind == LCPP_SCAN_INCLUSIVE)
+            scan_kernel<T, true><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, (const T*)carry_in, ticket, desc);
+        else
+            scan_kernel<T, false><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, (const T*)carry_in, ticket, desc);
+        count_launch();
+        return check_launch();
+    };
+    switch (dtype) {
+        case LCPP_I32: return go((int32_t)0);
+        case LCPP_U32: return go((uint32_t)0);
+        default: return go((float)0);
+    }
+}
+
+extern "C" lcpp_status lcpp_scan(int kind, int dtype, const void* in, void* out, uint64_t n,
+                                 void* temp, size_t temp_bytes, void* stream) {
+    return lcpp_scan_carry(kind, dtype, in, out, n, nullptr, temp, temp_bytes, stream);
+}
+
+extern "C" size_t lcpp_lookback_temp_bytes(uint64_t num_tiles) {
+    return SCAN_HDR + align_up((num_tiles ? num_tiles : 1) * sizeof(uint64_t), 256);
+}
+
+extern "C" lcpp_status lcpp_lookback_tiles(const uint32_t* aggregates, uint32_t* exclusive_out,
+                                           uint32_t* inclusive_out, uint64_t num_tiles,
+                                           void* temp, size_t temp_bytes, void* stream) {
+    if (num_tiles == 0) return LCPP_OK;
+    if (!aggregates || !exclusive_out || !inclusive_out || num_tiles > 0x7fffffffull) return LCPP_ERR_INVALID_ARG;
+    if (!temp || temp_bytes < lcpp_lookback_temp_bytes(num_tiles)) return LCPP_ERR_TEMP_TOO_SMALL;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(temp, 0, SCAN_HDR + num_tiles * 8, s) != cudaSuccess) return LCPP_ERR_CUDA;
+    lookback_tiles_kernel<<<(unsigned)num_tiles, 32, 0, s>>>(aggregates, exclusive_out, inclusive_out,
+                                                             (unsigned int*)temp,
+                                                             (uint64_t*)((char*)temp + SCAN_HDR));
+    count_launch();
+    return check_launch();
+}
+
+extern "C" lcpp_status lcpp_lookback_probe(const uint64_t* descriptors, uint64_t tile,
+                                           uint32_t* exclusive_out, void* stream) {
+    if (!descriptors || !exclusive_out) return LCPP_ERR_INVALID_ARG;
+    lookback_probe_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(descriptors, (int64_t)tile, exclusive_out);
+    count_launch();
+    return check_launch();
+}

@@ -1,0 +1,127 @@
+"""CPU oracle for LCPP's device primitives — TEST INFRASTRUCTURE ONLY.
+
+Used by tests/, __graft_entry__.smoke() (as the checker) and bench.py's
+cpu_baseline / reference arm (as the timed CPU baseline).  The product path
+(lc_parallel_primitive_b200) never imports this package.
+
+Parity pinning: the reference (LuisaCompute DSL) cannot be built here; the
+oracle is pinned on the reference tests' own std:: known answers, regenerated
+by tests/golden/refgen.cpp (see tests/test_oracle.py).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from .build import ORACLE_SO, build_oracle
+
+I32, U32, F32, I64, U64, F64, NONE = 0, 1, 2, 3, 4, 5, 15
+OP_SUM, OP_MIN, OP_MAX = 0, 1, 2
+
+_NP = {np.dtype(np.int32): I32, np.dtype(np.uint32): U32, np.dtype(np.float32): F32,
+       np.dtype(np.int64): I64, np.dtype(np.uint64): U64, np.dtype(np.float64): F64}
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not ORACLE_SO.exists():
+            build_oracle()
+        h = C.CDLL(str(ORACLE_SO))
+        vp, u64, i = C.c_void_p, C.c_uint64, C.c_int
+        h.oracle_reduce.argtypes = [i, i, vp, u64, vp]
+        h.oracle_scan.argtypes = [i, i, vp, u64, vp]
+        h.oracle_abs_prefix_f32.argtypes = [vp, u64, vp]
+        h.oracle_radix_sort.argtypes = [i, i, i, vp, vp, vp, vp, u64, i, i, i]
+        h.oracle_segment_reduce.argtypes = [i, i, vp, vp, u64, vp, vp]
+        h.oracle_reduce_sum_mt.argtypes = [i, vp, u64, vp, i]
+        h.oracle_scan_mt.argtypes = [i, i, vp, vp, u64, i]
+        h.oracle_segment_reduce_mt.argtypes = [i, i, vp, vp, u64, vp, vp, i]
+        for f in ("oracle_reduce", "oracle_scan", "oracle_abs_prefix_f32", "oracle_radix_sort",
+                  "oracle_segment_reduce", "oracle_reduce_sum_mt", "oracle_scan_mt",
+                  "oracle_segment_reduce_mt"):
+            getattr(h, f).restype = i
+        _lib = h
+    return _lib
+
+
+def _dt(a: np.ndarray) -> int:
+    return _NP[a.dtype]
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def _ok(rc, what):
+    if rc != 0:
+        raise ValueError(f"oracle {what} rejected its arguments")
+
+
+def reduce(op: int, x: np.ndarray):
+    """Integer: exact wrapped result in x.dtype.  Float: fp64 value."""
+    x = np.ascontiguousarray(x)
+    out = np.zeros(1, dtype=np.float64 if x.dtype.kind == "f" else x.dtype)
+    _ok(lib().oracle_reduce(op, _dt(x), _p(x), x.size, _p(out)), "reduce")
+    return out[0]
+
+
+def scan(inclusive: bool, x: np.ndarray) -> np.ndarray:
+    """u32/i32: exact wrapped prefixes in x.dtype.  f32: fp64 prefixes."""
+    x = np.ascontiguousarray(x)
+    out = np.empty(x.size, dtype=np.float64 if x.dtype == np.float32 else x.dtype)
+    _ok(lib().oracle_scan(int(inclusive), _dt(x), _p(x), x.size, _p(out)), "scan")
+    return out
+
+
+def abs_prefix(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size, dtype=np.float64)
+    lib().oracle_abs_prefix_f32(_p(x), x.size, _p(out))
+    return out
+
+
+def radix_sort(keys: np.ndarray, values: np.ndarray | None = None, descending=False, begin_bit=0,
+               end_bit=0, threads=1):
+    keys = np.ascontiguousarray(keys)
+    ko = np.empty_like(keys)
+    vo = None
+    vd = NONE
+    if values is not None:
+        values = np.ascontiguousarray(values)
+        vo = np.empty_like(values)
+        vd = _dt(values) if values.dtype in _NP else (U32 if values.itemsize == 4 else U64)
+    _ok(lib().oracle_radix_sort(_dt(keys), vd, int(descending), _p(keys), _p(ko), _p(values), _p(vo),
+                                keys.size, begin_bit, end_bit, threads), "radix_sort")
+    return (ko, vo) if values is not None else ko
+
+
+def segment_reduce(op: int, x: np.ndarray, begin: np.ndarray, end: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    begin = np.ascontiguousarray(begin, dtype=np.uint32)
+    end = np.ascontiguousarray(end, dtype=np.uint32)
+    out = np.empty(begin.size, dtype=np.float64 if x.dtype.kind == "f" else x.dtype)
+    _ok(lib().oracle_segment_reduce(op, _dt(x), _p(x), _p(out), begin.size, _p(begin), _p(end)),
+        "segment_reduce")
+    return out
+
+
+# ---- multi-threaded baselines (element-type arithmetic) --------------------
+def reduce_sum_mt(x: np.ndarray, threads: int):
+    out = np.zeros(1, dtype=x.dtype)
+    _ok(lib().oracle_reduce_sum_mt(_dt(x), _p(x), x.size, _p(out), threads), "reduce_sum_mt")
+    return out[0]
+
+
+def scan_mt(inclusive: bool, x: np.ndarray, out: np.ndarray, threads: int):
+    _ok(lib().oracle_scan_mt(int(inclusive), _dt(x), _p(x), _p(out), x.size, threads), "scan_mt")
+    return out
+
+
+def segment_reduce_mt(op: int, x, begin, end, out, threads: int):
+    _ok(lib().oracle_segment_reduce_mt(op, _dt(x), _p(x), _p(out), begin.size, _p(begin), _p(end), threads),
+        "segment_reduce_mt")
+    return out

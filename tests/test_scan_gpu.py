@@ -1,0 +1,75 @@
+"""DeviceScan parity on the GPU against the CPU oracle and the reference tests'
+known answers (tests/device_scan_test.cpp)."""
+import numpy as np
+import pytest
+
+import oracle
+from lc_parallel_primitive_b200 import datagen as G
+from tests.helpers import abi_scan, assert_float_sum_close, to_host
+
+pytestmark = pytest.mark.gpu
+
+
+def test_reference_scan_of_ones(cuda):
+    # tests/device_scan_test.cpp:67-108: uint Exclusive/InclusiveSum of all
+    # ones, n = 2^0 .. 2^23, compared with std::exclusive_scan/inclusive_scan.
+    import torch
+    from lc_parallel_primitive_b200 import CommandList, DeviceScan, Stream, synchronize, temp_buffer
+
+    scanner = DeviceScan(256, 32, 4)
+    stream = Stream()
+    scanner.create(None, stream)
+    cmdlist = CommandList()
+    for i in range(24):
+        n = 1 << i
+        d_in = torch.ones(n, dtype=torch.int32, device=cuda).view(torch.uint32)
+        ex = torch.empty(n, dtype=torch.uint32, device=cuda)
+        inc = torch.empty(n, dtype=torch.uint32, device=cuda)
+        temp = temp_buffer(DeviceScan.GetTempStorageBytes(n, torch.uint32))
+        scanner.ExclusiveSum(cmdlist, temp, d_in, ex, n)
+        stream << cmdlist.commit() << synchronize()
+        scanner.InclusiveSum(cmdlist, temp, d_in, inc, n)
+        stream << cmdlist.commit() << synchronize()
+        iota = np.arange(n, dtype=np.uint32)
+        assert np.array_equal(to_host(ex), iota), n
+        assert np.array_equal(to_host(inc), iota + 1), n
+
+
+SIZES = [1, 2, 31, 32, 33, 1023, 1024, 1025, 8191, 8192, 8193, 3 * 8192 + 17, 100000, (1 << 20) + 1]
+
+
+@pytest.mark.parametrize("inclusive", [False, True])
+@pytest.mark.parametrize("dtype", [np.uint32, np.int32])
+def test_integer_scan_bit_exact(cuda, inclusive, dtype):
+    for i, n in enumerate(SIZES):
+        x = G.u32(n, seed=100 + i).view(dtype)  # full range: exercises wraparound
+        got = abi_scan(inclusive, x, offset_elems=i % 3)
+        assert np.array_equal(got, oracle.scan(inclusive, x)), n
+
+
+@pytest.mark.parametrize("inclusive", [False, True])
+def test_float_scan_tolerance(cuda, inclusive):
+    for i, n in enumerate(SIZES):
+        x = G.f32_normal(n, seed=200 + i)
+        got = abi_scan(inclusive, x, offset_elems=i % 2)
+        assert_float_sum_close(got, oracle.scan(inclusive, x), oracle.abs_prefix(x))
+
+
+def test_in_place(cuda):
+    x = G.u32_below(123457, 16, seed=7)
+    got = abi_scan(False, x, in_place=True)
+    assert np.array_equal(got, oracle.scan(False, x))
+
+
+def test_config2_exclusive_u32_full(cuda):
+    # 2^28 uint32 uniform in [0,16), bit-exact.
+    x = G.u32_below(1 << 28, 16, seed=1, stream=5)
+    got = abi_scan(False, x)
+    assert np.array_equal(got, oracle.scan(False, x))
+
+
+def test_config2_inclusive_f32_full(cuda):
+    # 2^28 float32 N(0,1); |y-ref| <= 1e-5*max(|ref|, sum|x|*2^-10).
+    x = G.f32_normal(1 << 28, seed=1, stream=5)
+    got = abi_scan(True, x)
+    assert_float_sum_close(got, oracle.scan(True, x), oracle.abs_prefix(x))
