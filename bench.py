@@ -37,6 +37,9 @@ sys.path.insert(0, str(ROOT))
 N_SORT = 1 << 28
 METRIC = "Onesweep sort Gkeys/s; scan/reduce HBM GB/s (% of ~8 TB/s) at 1/2/4/8 B200"
 UNIT = "Gkeys/s"
+# DRAM bytes per pair per onesweep launch from the committed ncu capture
+# (profiles/), or None before one exists.
+TRAFFIC_PER_PAIR_PASS = None
 
 
 def load_peaks():
@@ -159,6 +162,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the scan/reduce/segment lines")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end timing")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--n-log2", type=int, default=28, help="pairs per GPU = 2^n (profiling runs use less)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -189,7 +195,7 @@ def main():
     sh = stream.cuda_stream
 
     # ---- inputs (host, pinned) ------------------------------------------------
-    n = N_SORT
+    n = 1 << args.n_log2
     keys_np = G.u32(n, seed=1 + rank, stream=7)
     h_keys = torch.from_numpy(keys_np.view(np.int32)).pin_memory()
     h_vals = torch.from_numpy(G.iota_u32(n).view(np.int32)).pin_memory()
@@ -261,6 +267,66 @@ def main():
     hist_avg_ms = prof["rs_histogram"][1] / max(prof["rs_histogram"][0], 1)
 
     # ---- e2e through the public API with host buffers ---------------------------
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_keys, d_vals,
+                      d_keys_out, d_vals_out, d_temp, args, barrier, max_over_ranks)
+
+    # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        sample = min(1 << 24, n)
+        ks, vs = keys_np[:sample].copy(), np.arange(sample, dtype=np.uint32)
+        oracle.radix_sort(ks, vs, threads=cores)
+        reps, t0 = 3, time.perf_counter()
+        for _ in range(reps):
+            oracle.radix_sort(ks, vs, threads=cores)
+        sec = (time.perf_counter() - t0) / reps
+        cpu = {"value": sample / sec / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{sample} of the 2^28 pairs, LSD radix sort (oracle/), {reps} reps"}
+
+    extras = {}
+    if not args.no_extras:
+        del h_keys_out, h_vals_out
+        extras = run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u32", "data": "synthetic (PCG32 seeded, uniform u32 keys, iota values)",
+            "config": {"workload": f"DeviceRadixSort::SortPairs, n=2^{args.n_log2} u32 keys + u32 values per GPU (BASELINE config 3)",
+                       "n_per_gpu": n, "parallelism": f"independent shards x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs 2 GiB per step > 126 MB L2 (no flush needed)",
+                       "algorithmic_bytes_per_pair": 68},
+            "roofline": {"bound": "hbm", "kernel": "rs_onesweep_kernel (one 8-bit pass)",
+                         "achieved": os_achieved, "peak": peak, "unit": "GB/s", "frac": os_achieved / peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                         "traffic": TRAFFIC_PER_PAIR_PASS * n if TRAFFIC_PER_PAIR_PASS else None,
+                         "avg_launch_ms": os_avg_ms, "bytes_per_launch": os_bytes,
+                         "whole_sort_frac": (68 * n / (ms * 1e-3) / 1e9) / peak},
+            "kernels": {k: {"launches": c, "total_ms": t} for k, (c, t) in prof.items()},
+            "histogram_avg_ms": hist_avg_ms,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "extras": extras,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_keys, d_vals, d_keys_out,
+            d_vals_out, d_temp, args, barrier, max_over_ranks):
+    """Same metric through the public API (DeviceRadixSort.SortPairs recorded
+    into a CommandList and committed to a Stream), with the step's inputs
+    copied from pinned host memory and the sorted pairs copied back."""
+    from lc_parallel_primitive_b200.primitives import CommandList, DeviceRadixSort, Stream, synchronize
+
     sorter = DeviceRadixSort()
     sorter.create(None)
     api_stream = Stream(stream)
@@ -284,56 +350,10 @@ def main():
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    e2e_value = world * n / (e2e_ms * 1e-3) / 1e9
     assert np.array_equal(h_vals_out[:1000].numpy(), d_vals_out[:1000].cpu().numpy())
-
-    # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------
-    cpu = None
-    if rank == 0 and world == 1:
-        cores = os.cpu_count() or 1
-        sample = 1 << 24
-        ks, vs = keys_np[:sample].copy(), np.arange(sample, dtype=np.uint32)
-        oracle.radix_sort(ks, vs, threads=cores)
-        reps, t0 = 3, time.perf_counter()
-        for _ in range(reps):
-            oracle.radix_sort(ks, vs, threads=cores)
-        sec = (time.perf_counter() - t0) / reps
-        cpu = {"value": sample / sec / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{sample} of the 2^28 pairs, LSD radix sort (oracle/), {reps} reps"}
-
-    extras = {}
-    if not args.no_extras:
-        del h_keys_out, h_vals_out
-        extras = run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier)
-
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "u32", "data": "synthetic (PCG32 seeded, uniform u32 keys, iota values)",
-            "config": {"workload": "DeviceRadixSort::SortPairs, n=2^28 u32 keys + u32 values per GPU (BASELINE config 3)",
-                       "n_per_gpu": n, "parallelism": f"independent shards x{world}" if world > 1 else "single GPU",
-                       "l2": "inputs 2 GiB per step > 126 MB L2 (no flush needed)",
-                       "algorithmic_bytes_per_pair": 68},
-            "roofline": {"bound": "hbm", "kernel": "rs_onesweep_kernel (one 8-bit pass)",
-                         "achieved": os_achieved, "peak": peak, "unit": "GB/s", "frac": os_achieved / peak,
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-                         "traffic": None, "avg_launch_ms": os_avg_ms, "bytes_per_launch": os_bytes,
-                         "whole_sort_frac": (68 * n / (ms * 1e-3) / 1e9) / peak},
-            "kernels": {k: {"launches": c, "total_ms": t} for k, (c, t) in prof.items()},
-            "histogram_avg_ms": hist_avg_ms,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 8 * n,
-                    "ms_per_step": e2e_ms, "api": "DeviceRadixSort.SortPairs via CommandList/Stream",
-                    "steps": e2e_steps},
-            "gpu_launches": int(launches),
-            "clocks": clocks.summary(),
-            "cpu_baseline": cpu,
-            "extras": extras,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
-    return 0
+    return {"value": world * n / (e2e_ms * 1e-3) / 1e9, "unit": UNIT, "h2d_bytes_per_step": 8 * n,
+            "d2h_bytes_per_step": 8 * n, "ms_per_step": e2e_ms,
+            "api": "DeviceRadixSort.SortPairs via CommandList/Stream", "steps": e2e_steps}
 
 
 def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier):
@@ -396,7 +416,7 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
     t = torch.empty(tb, dtype=torch.uint8, device=dev)
     ms = timeit(lambda: L.check(lib.lcpp_segment_reduce(0, L.F32, xs.data_ptr(), o.data_ptr(), S, b.data_ptr(),
                                                         e.data_ptr(), t.data_ptr(), tb, sh)), 20)
-    byts = 4 * N + 4 * (S + 1) + 4 * S + 4 * S
+    byts = 4 * N + 4 * (S + 1) + 4 * S  # values + CSR offsets + outputs
     out["segment_sum_f32_2p27_2p20"] = {"ms": ms, "GB/s": byts / ms / 1e6, "frac": byts / ms / 1e6 / peak}
     return out
 

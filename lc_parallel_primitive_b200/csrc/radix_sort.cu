@@ -37,6 +37,7 @@ constexpr int RS_WARPS = RS_THREADS / 32;
 constexpr int RS_MAX_PASSES = 8;
 constexpr int HIST_THREADS = 512;
 constexpr int HIST_CTAS_PER_SM = 2;
+constexpr int RS_LB_WINDOW = 8;  // predecessor words loaded per look-back step
 
 template <typename KB> struct RsItems;
 template <> struct RsItems<uint32_t> { static constexpr int value = 16; };
@@ -78,44 +79,63 @@ rs_histogram_kernel(const KB* __restrict__ keys, uint64_t n, uint32_t* __restric
     __syncthreads();
     const int lane = threadIdx.x & 31;
 
-    auto count_key = [&](KB k, bool valid) {
-        const KB o = ordered_bits<KB, KIND, DESC>(k);
+    // Count the digits of the N keys in k[] (all passes).  When every lane of
+    // the warp holds N valid keys with one and the same digit, lane 0 adds
+    // 32*N at once (skewed inputs would otherwise serialise on one counter).
+    auto count_keys = [&](const KB* k, int N, bool valid) {
+        KB o[16 / sizeof(KB)];
+        for (int v = 0; v < N; ++v) o[v] = ordered_bits<KB, KIND, DESC>(k[v]);
 #pragma unroll
         for (uint32_t p = 0; p < RS_MAX_PASSES; ++p) {
             if (p >= passes) break;
             const uint32_t shift = begin_bit + p * RS_BITS;
-            const uint32_t nb = min((uint32_t)RS_BITS, end_bit - shift);
-            const uint32_t d = (uint32_t)(o >> shift) & ((1u << nb) - 1u);
-            const uint32_t d0 = __shfl_sync(0xffffffffu, d, 0);
-            const bool all_valid = __all_sync(0xffffffffu, valid);
-            if (all_valid && __all_sync(0xffffffffu, d == d0)) {
-                if (lane == 0) atomicAdd(&sh[p][d0], 32u);
+            const uint32_t mask = (1u << min((uint32_t)RS_BITS, end_bit - shift)) - 1u;
+            uint32_t d[16 / sizeof(KB)];
+            bool same = valid;
+            for (int v = 0; v < N; ++v) {
+                d[v] = (uint32_t)(o[v] >> shift) & mask;
+                same = same && d[v] == d[0];
+            }
+            const uint32_t d00 = __shfl_sync(0xffffffffu, d[0], 0);
+            if (__all_sync(0xffffffffu, same && d[0] == d00)) {
+                if (lane == 0) atomicAdd(&sh[p][d00], 32u * N);
             } else if (valid) {
-                atomicAdd(&sh[p][d], 1u);
+                for (int v = 0; v < N; ++v) atomicAdd(&sh[p][d[v]], 1u);
             }
         }
     };
 
     constexpr int VEC = 16 / sizeof(KB);
+    constexpr int HU = 4;  // 16-byte loads in flight per thread
     const bool aligned = (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
     const uint64_t nvec = aligned ? n / VEC : 0;
     const uint4* vk = reinterpret_cast<const uint4*>(keys);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     // Whole warps iterate together so the warp-uniform fast path stays legal.
     const uint64_t nvec_pad = (nvec + 31) / 32 * 32;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec_pad; i += stride) {
-        const bool valid = i < nvec;
-        uint4 q = valid ? ld_stream(vk + i) : make_uint4(0, 0, 0, 0);
-        const KB* e = reinterpret_cast<const KB*>(&q);
+    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + (HU - 1) * stride < nvec_pad; i += HU * stride) {
+        uint4 q[HU];
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) count_key(e[v], valid);
+        for (int u = 0; u < HU; ++u) {
+            const uint64_t j = i + u * stride;
+            q[u] = j < nvec ? ld_stream(vk + j) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < HU; ++u) count_keys(reinterpret_cast<const KB*>(&q[u]), VEC, i + u * stride < nvec);
+    }
+    for (; i < nvec_pad; i += stride) {
+        const bool valid = i < nvec;
+        const uint4 q = valid ? ld_stream(vk + i) : make_uint4(0, 0, 0, 0);
+        count_keys(reinterpret_cast<const KB*>(&q), VEC, valid);
     }
     // Scalar tail (all keys when the base is not 16-byte aligned).
     const uint64_t t0 = nvec * VEC;
     const uint64_t ntail_pad = (n - t0 + 31) / 32 * 32;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ntail_pad; i += stride) {
+    for (i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ntail_pad; i += stride) {
         const bool valid = t0 + i < n;
-        count_key(valid ? keys[t0 + i] : KB(0), valid);
+        const KB k = valid ? keys[t0 + i] : KB(0);
+        count_keys(&k, 1, valid);
     }
     __syncthreads();
     for (uint32_t i = threadIdx.x; i < passes * RS_DIGITS; i += blockDim.x) {
@@ -279,23 +299,35 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
         if (tile == 0) {
             excl = a.bins[tid];
         } else {
+            // Walk back over predecessors RS_LB_WINDOW at a time: the window's
+            // words are loaded together (independent loads in flight), then
+            // consumed nearest first until an inclusive word ends the walk.
             W acc = 0;
-            uint64_t pt = tile - 1;
+            int64_t pt = (int64_t)tile - 1;
             uint32_t spins = 0;
             const uint32_t limit = g_spin_limit;
-            while (true) {
-                W w = lb_load(lb + pt * RS_DIGITS + tid);
-                while ((w & (F::PART | F::INCL)) == 0) {
-                    if (++spins > limit) {
-                        set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
-                        break;
+            bool done = false;
+            while (!done) {
+                W w[RS_LB_WINDOW];
+#pragma unroll
+                for (int j = 0; j < RS_LB_WINDOW; ++j)
+                    w[j] = pt - j >= 0 ? lb_load(lb + (uint64_t)(pt - j) * RS_DIGITS + tid) : F::INCL;
+#pragma unroll
+                for (int j = 0; j < RS_LB_WINDOW; ++j) {
+                    if (done) break;
+                    while ((w[j] & (F::PART | F::INCL)) == 0) {
+                        if (++spins > limit) {
+                            set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
+                            w[j] = F::INCL;  // give up: treat as resolved
+                            break;
+                        }
+                        if (spins > 4) __nanosleep(spins < 64 ? 32 : 256);
+                        w[j] = lb_load(lb + (uint64_t)(pt - j) * RS_DIGITS + tid);
                     }
-                    if (spins > 4) __nanosleep(spins < 64 ? 32 : 256);
-                    w = lb_load(lb + pt * RS_DIGITS + tid);
+                    acc += w[j] & F::MASK;
+                    if (w[j] & F::INCL) done = true;
                 }
-                acc += w & F::MASK;
-                if ((w & F::INCL) || pt == 0 || spins > limit) break;
-                --pt;
+                pt -= RS_LB_WINDOW;
             }
             excl = acc;
             lb_store(lb + tile * RS_DIGITS + tid, F::INCL | (excl + total));

@@ -162,11 +162,10 @@ scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in,
         const T c0 = carry_in ? *carry_in : T(0);
         const T block_excl = tile_prefix<T>(desc, tile, aggregate, c0);
         __syncwarp();
-        if (lane < SCAN_WARPS) {
-            T wex = __shfl_up_sync(0xffffffffu, incl, 1);
-            if (lane == 0) wex = T(0);
-            s_warp[lane] = add(block_excl, wex);
-        }
+        // All 32 lanes take part in the shuffle; only 16 store.
+        T wex = __shfl_up_sync(0xffffffffu, incl, 1);
+        if (lane == 0) wex = T(0);
+        if (lane < SCAN_WARPS) s_warp[lane] = add(block_excl, wex);
     }
     __syncthreads();
     const T wbase = s_warp[warp];

@@ -69,7 +69,7 @@ def test_config2_exclusive_u32_full(cuda):
 
 
 def test_config2_inclusive_f32_full(cuda):
-    # 2^28 float32 N(0,1); |y-ref| <= 1e-5*max(|ref|, sum|x|*2^-10).
+    # 2^28 float32 N(0,1); |y-ref| <= 1e-5*max(|ref|, sum|x|*2^-6).
     x = G.f32_normal(1 << 28, seed=1, stream=5)
     got = abi_scan(True, x)
     assert_float_sum_close(got, oracle.scan(True, x), oracle.abs_prefix(x))
