@@ -243,7 +243,15 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
     for (int i = 0; i < ITEMS; ++i) {
         const uint32_t li = wbase + i * 32 + lane;
         const uint32_t d = li < num_valid ? digit_of<KB, KIND, DESC>(key[i], a.shift, a.mask) : (RS_DIGITS - 1);
-        const uint32_t peers = __match_any_sync(0xffffffffu, d);
+        // Lanes holding the same digit: one ballot per digit bit (cheaper
+        // than match.any, which issues on the low-throughput ADU pipe).
+        uint32_t peers = 0xffffffffu;
+#pragma unroll
+        for (int b = 0; b < RS_BITS; ++b) {
+            const bool bit = (d >> b) & 1u;
+            const uint32_t m = __ballot_sync(0xffffffffu, bit);
+            peers &= bit ? m : ~m;
+        }
         const int leader = 31 - __clz(peers);
         uint32_t old = 0;
         if (lane == leader) old = atomicAdd(wc + d, (uint32_t)__popc(peers));
