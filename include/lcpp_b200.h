@@ -131,6 +131,21 @@ lcpp_status lcpp_segment_reduce_fixed(int op, int dtype, const void* in, void* o
                                       uint64_t num_segments, uint64_t segment_size,
                                       void* stream);
 
+/* ---- DeviceScan without temp storage ----------------------------------
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory when they scan (allocator or memory-pool callbacks, plug-ins that
+ * only receive their input/output buffers, real-time paths that forbid
+ * allocation after start-up): same result as lcpp_scan, with the scratch
+ * taken from a fixed ~512 KiB device array inside the library instead of a
+ * caller temp buffer.  n <= lcpp_scan_noalloc_max_items() (2^29), larger n
+ * returns LCPP_ERR_INVALID_ARG.  The array is shared by all calls on a device:
+ * calls that overlap on the GPU race and must be serialized.  The first call
+ * on a device looks up the array's address (cudaGetSymbolAddress); make it
+ * before any stream capture.  Allocates nothing. */
+uint64_t    lcpp_scan_noalloc_max_items(void);
+lcpp_status lcpp_scan_noalloc(int kind, int dtype, const void* in, void* out, uint64_t n,
+                              void* stream);
+
 /* ---- Device error word --------------------------------------------------
  * Synchronizes `stream`, returns the first device-side error latched since
  * the last call on the current device (LCPP_OK if none) and clears it.  The

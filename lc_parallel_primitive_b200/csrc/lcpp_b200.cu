@@ -5,3 +5,4 @@
 #include "scan.cu"
 #include "radix_sort.cu"
 #include "segment_reduce.cu"
+#include "scan_noalloc.cu"
