@@ -199,6 +199,13 @@ constexpr size_t rs_smem_bytes() {
            (size_t)RS_WARPS * RS_DIGITS * 4 + RS_DIGITS * 4 * 2 + 64;
 }
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 template <typename KB, typename VB, typename W, int KIND, bool DESC>
 __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
     constexpr int ITEMS = RsItems<KB>::value;
@@ -233,6 +240,21 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
     for (int i = 0; i < ITEMS; ++i) {
         const uint32_t li = wbase + i * 32 + lane;
         key[i] = li < num_valid ? ldcs(kin + tile_base + li) : KB(0);
+    }
+    // ---- values of a full tile: asynchronous copy into shared memory (input
+    // order) that lands while the keys are ranked ------------------------------
+    const VB* vin = reinterpret_cast<const VB*>(a.vals_in);
+    bool v_staged = false;
+    if constexpr (HAS_V) {
+        v_staged = num_valid == (uint32_t)TILE && (reinterpret_cast<uintptr_t>(vin + tile_base) & 15) == 0;
+        if (v_staged) {
+            constexpr int CHUNKS = TILE * (int)sizeof(VB) / 16;
+            const char* src = reinterpret_cast<const char*>(vin + tile_base);
+            char* dst = reinterpret_cast<char*>(s_vals);
+#pragma unroll
+            for (int c = tid; c < CHUNKS; c += RS_THREADS) cp_async16(dst + c * 16, src + c * 16);
+            cp_async_commit();
+        }
     }
 
     // ---- stable in-warp rank ---------------------------------------------------
@@ -345,12 +367,19 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
 
     // ---- values into shared memory in digit order -----------------------------
     if constexpr (HAS_V) {
-        const VB* vin = reinterpret_cast<const VB*>(a.vals_in);
         VB val[ITEMS];
+        if (v_staged) {
+            cp_async_wait_all();
+            __syncthreads();  // every thread's chunks have landed
 #pragma unroll
-        for (int i = 0; i < ITEMS; ++i) {
-            const uint32_t li = wbase + i * 32 + lane;
-            if (li < num_valid) val[i] = ldcs(vin + tile_base + li);
+            for (int i = 0; i < ITEMS; ++i) val[i] = s_vals[wbase + i * 32 + lane];
+            __syncthreads();  // staging fully read before it is overwritten
+        } else {
+#pragma unroll
+            for (int i = 0; i < ITEMS; ++i) {
+                const uint32_t li = wbase + i * 32 + lane;
+                if (li < num_valid) val[i] = ldcs(vin + tile_base + li);
+            }
         }
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
