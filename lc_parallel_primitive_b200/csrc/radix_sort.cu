@@ -196,7 +196,7 @@ constexpr size_t rs_smem_bytes() {
     constexpr int TILE = RS_THREADS * RsItems<KB>::value;
     return (size_t)TILE * sizeof(KB) +
            (std::is_same<VB, NoValue>::value ? 0 : (size_t)TILE * sizeof(VB)) +
-           (size_t)RS_WARPS * RS_DIGITS * 4 + RS_DIGITS * 4 * 2 + 64;
+           (size_t)RS_WARPS * RS_DIGITS * 4 * 2 + RS_DIGITS * 4 * 2 + 64;
 }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
@@ -221,10 +221,11 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
     uint32_t* s_wc = reinterpret_cast<uint32_t*>(p);          // [RS_WARPS][256]
     uint32_t* s_gbase = s_wc + RS_WARPS * RS_DIGITS;         // [256]
     uint32_t* s_misc = s_gbase + RS_DIGITS;                  // [0] tile id, [1..8] warp sums
+    uint32_t* s_wm = s_misc + 16;                            // [RS_WARPS][256] lane masks per digit
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) s_misc[0] = atomicAdd(a.ticket, 1u);
-    for (int i = tid; i < RS_WARPS * RS_DIGITS; i += RS_THREADS) s_wc[i] = 0;
+    for (int i = tid; i < RS_WARPS * RS_DIGITS; i += RS_THREADS) s_wc[i] = s_wm[i] = 0;
     __syncthreads();
     const uint64_t tile = s_misc[0];
     const uint64_t tile_base = tile * TILE;
@@ -259,25 +260,29 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
 
     // ---- stable in-warp rank ---------------------------------------------------
     uint32_t* wc = s_wc + warp * RS_DIGITS;
+    uint32_t* wm = s_wm + warp * RS_DIGITS;
     const uint32_t lt = lanemask_lt();
     uint32_t rank[ITEMS];  // (rank within warp & digit) | digit << 16
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
         const uint32_t li = wbase + i * 32 + lane;
         const uint32_t d = li < num_valid ? digit_of<KB, KIND, DESC>(key[i], a.shift, a.mask) : (RS_DIGITS - 1);
-        // Lanes holding the same digit: one ballot per digit bit (cheaper
-        // than match.any, which issues on the low-throughput ADU pipe).
-        uint32_t peers = 0xffffffffu;
-#pragma unroll
-        for (int b = 0; b < RS_BITS; ++b) {
-            const bool bit = (d >> b) & 1u;
-            const uint32_t m = __ballot_sync(0xffffffffu, bit);
-            peers &= bit ? m : ~m;
-        }
+        // Lanes holding the same digit: each lane sets its bit in the warp's
+        // mask word for its digit, reads the word back, and the highest lane
+        // of the group advances the warp's counter and clears the word.
+        atomicOr(wm + d, 1u << lane);
+        __syncwarp();
+        const uint32_t peers = wm[d];
         const int leader = 31 - __clz(peers);
+        __syncwarp();
         uint32_t old = 0;
-        if (lane == leader) old = atomicAdd(wc + d, (uint32_t)__popc(peers));
+        if (lane == leader) {
+            old = wc[d];
+            wc[d] = old + __popc(peers);
+            wm[d] = 0;
+        }
         old = __shfl_sync(0xffffffffu, old, leader);
+        __syncwarp();
         rank[i] = (old + __popc(peers & lt)) | (d << 16);
     }
     __syncthreads();
