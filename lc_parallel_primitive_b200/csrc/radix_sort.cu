@@ -258,36 +258,18 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
         }
     }
 
-    // ---- stable in-warp rank ---------------------------------------------------
+    // ---- early counts: per-warp digit histogram of the tile -------------------
     uint32_t* wc = s_wc + warp * RS_DIGITS;
     uint32_t* wm = s_wm + warp * RS_DIGITS;
-    const uint32_t lt = lanemask_lt();
-    uint32_t rank[ITEMS];  // (rank within warp & digit) | digit << 16
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
         const uint32_t li = wbase + i * 32 + lane;
         const uint32_t d = li < num_valid ? digit_of<KB, KIND, DESC>(key[i], a.shift, a.mask) : (RS_DIGITS - 1);
-        // Lanes holding the same digit: each lane sets its bit in the warp's
-        // mask word for its digit, reads the word back, and the highest lane
-        // of the group advances the warp's counter and clears the word.
-        atomicOr(wm + d, 1u << lane);
-        __syncwarp();
-        const uint32_t peers = wm[d];
-        const int leader = 31 - __clz(peers);
-        __syncwarp();
-        uint32_t old = 0;
-        if (lane == leader) {
-            old = wc[d];
-            wc[d] = old + __popc(peers);
-            wm[d] = 0;
-        }
-        old = __shfl_sync(0xffffffffu, old, leader);
-        __syncwarp();
-        rank[i] = (old + __popc(peers & lt)) | (d << 16);
+        atomicAdd(wc + d, 1u);
     }
     __syncthreads();
 
-    // ---- per-digit tile counts, partial publish, tile-local digit offsets ---
+    // ---- tile digit totals: publish at once, then tile-local digit offsets ---
     W* lb = reinterpret_cast<W*>(a.lookback);
     uint32_t total = 0;
     if (tid < RS_DIGITS) {
@@ -311,6 +293,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
     if (tid < RS_DIGITS) {
         for (int w = 0; w < warp; ++w) off += s_misc[1 + w];
         off += incl - total;
+        // each warp's counter starts at the tile position of its first key of d
         uint32_t run = off;
 #pragma unroll
         for (int w = 0; w < RS_WARPS; ++w) {
@@ -321,14 +304,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
     }
     __syncthreads();
 
-    // ---- keys into shared memory in digit order -------------------------------
-#pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-        const uint32_t d = rank[i] >> 16;
-        s_keys[wc[d] + (rank[i] & 0xffffu)] = key[i];
-    }
-
-    // ---- per-digit look-back (threads 0..255) ---------------------------------
+    // ---- per-digit look-back (warps 0..7; the other warps rank meanwhile) ----
     if (tid < RS_DIGITS) {
         W excl;
         if (tile == 0) {
@@ -356,7 +332,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
                             w[j] = F::INCL;  // give up: treat as resolved
                             break;
                         }
-                        if (spins > 4) __nanosleep(spins < 64 ? 32 : 256);
+                        __nanosleep(spins < 16 ? 64 : 256);  // leave issue slots to the ranking warps
                         w[j] = lb_load(lb + (uint64_t)(pt - j) * RS_DIGITS + tid);
                     }
                     acc += w[j] & F::MASK;
@@ -368,6 +344,33 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
             lb_store(lb + tile * RS_DIGITS + tid, F::INCL | (excl + total));
         }
         s_gbase[tid] = (uint32_t)excl - off;
+    }
+
+    // ---- stable rank: keys straight to their tile position in shared memory --
+    const uint32_t lt = lanemask_lt();
+    uint32_t pos[ITEMS];
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+        const uint32_t li = wbase + i * 32 + lane;
+        const uint32_t d = li < num_valid ? digit_of<KB, KIND, DESC>(key[i], a.shift, a.mask) : (RS_DIGITS - 1);
+        // Lanes holding the same digit: each lane sets its bit in the warp's
+        // mask word for its digit, reads the word back, and the highest lane
+        // of the group advances the warp's running position and clears the word.
+        atomicOr(wm + d, 1u << lane);
+        __syncwarp();
+        const uint32_t peers = wm[d];
+        const int leader = 31 - __clz(peers);
+        __syncwarp();
+        uint32_t old = 0;
+        if (lane == leader) {
+            old = wc[d];
+            wc[d] = old + __popc(peers);
+            wm[d] = 0;
+        }
+        old = __shfl_sync(0xffffffffu, old, leader);
+        __syncwarp();
+        pos[i] = old + __popc(peers & lt);
+        s_keys[pos[i]] = key[i];
     }
 
     // ---- values into shared memory in digit order -----------------------------
@@ -389,8 +392,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
             const uint32_t li = wbase + i * 32 + lane;
-            const uint32_t d = rank[i] >> 16;
-            if (li < num_valid) s_vals[wc[d] + (rank[i] & 0xffffu)] = val[i];
+            if (li < num_valid) s_vals[pos[i]] = val[i];
         }
     }
     __syncthreads();
