@@ -165,6 +165,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end timing")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--n-log2", type=int, default=28, help="pairs per GPU = 2^n (profiling runs use less)")
+    ap.add_argument("--extras-scale", type=int, default=0,
+                    help="shrink the scan/reduce/segment inputs by 2^k (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -289,7 +291,7 @@ def main():
     extras = {}
     if not args.no_extras:
         del h_keys_out, h_vals_out
-        extras = run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier)
+        extras = run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier, args.extras_scale)
 
     if rank == 0:
         line = {
@@ -356,7 +358,7 @@ def run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_k
             "api": "DeviceRadixSort.SortPairs via CommandList/Stream", "steps": e2e_steps}
 
 
-def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier):
+def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier, shrink=0):
     """Scan (config 2), reduce (config 1) and segment reduce (config 4), each
     timed with CUDA events; GB/s from algorithmic bytes."""
     stream = torch.cuda.current_stream()
@@ -381,22 +383,22 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
         return max_over_ranks(tot / iters)
 
     # scan: 2^28 u32 exclusive, 2^28 f32 inclusive
-    n = 1 << 28
+    n = 1 << (28 - shrink)
     x = torch.from_numpy(G.u32_below(n, 16, seed=1, stream=5).view(np.int32)).to(dev)
     y = torch.empty_like(x)
     tb = lib.lcpp_scan_temp_bytes(L.U32, n)
     t = torch.empty(tb, dtype=torch.uint8, device=dev)
     ms = timeit(lambda: L.check(lib.lcpp_scan(0, L.U32, x.data_ptr(), y.data_ptr(), n, t.data_ptr(), tb, sh)), 20)
-    out["scan_exclusive_u32_2p28"] = {"ms": ms, "GB/s": 8 * n / ms / 1e6, "frac": 8 * n / ms / 1e6 / peak}
+    out[f"scan_exclusive_u32_2p{28 - shrink}"] = {"ms": ms, "GB/s": 8 * n / ms / 1e6, "frac": 8 * n / ms / 1e6 / peak}
     xf = torch.from_numpy(G.f32_normal(n, seed=1, stream=5)).to(dev)
     ms = timeit(lambda: L.check(lib.lcpp_scan(1, L.F32, xf.data_ptr(), y.data_ptr(), n, t.data_ptr(), tb, sh)), 20)
-    out["scan_inclusive_f32_2p28"] = {"ms": ms, "GB/s": 8 * n / ms / 1e6, "frac": 8 * n / ms / 1e6 / peak}
+    out[f"scan_inclusive_f32_2p{28 - shrink}"] = {"ms": ms, "GB/s": 8 * n / ms / 1e6, "frac": 8 * n / ms / 1e6 / peak}
     del xf, y, t
 
     # reduce: 2^24 int32 (L2 flushed between iterations) and 2^28 int32
-    for logn in (24, 28):
+    for logn in (24 - shrink, 28 - shrink):
         n = 1 << logn
-        xr = x[:n] if logn == 28 else torch.from_numpy(G.i32_range(n, -1000, 1000, seed=1, stream=3)).to(dev)
+        xr = x[:n] if logn == 28 - shrink else torch.from_numpy(G.i32_range(n, -1000, 1000, seed=1, stream=3)).to(dev)
         o = torch.empty(1, dtype=torch.int32, device=dev)
         tb = lib.lcpp_reduce_temp_bytes(L.I32, n)
         t = torch.empty(tb, dtype=torch.uint8, device=dev)
@@ -406,7 +408,7 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
     del x
 
     # segment reduce: 2^27 f32, 2^20 lognormal segments
-    N, S = 1 << 27, 1 << 20
+    N, S = 1 << (27 - shrink), 1 << (20 - shrink)
     off = G.lognormal_offsets(S, N, seed=1, stream=9)
     xs = torch.from_numpy(G.f32_unit(N, seed=1, stream=10)).to(dev)
     b = torch.from_numpy(off[:-1].view(np.int32).copy()).to(dev)

@@ -191,12 +191,12 @@ struct RsPass {
     uint32_t* ticket;       // zeroed
 };
 
-template <typename KB, typename VB>
+template <typename KB, typename VB, int THREADS>
 constexpr size_t rs_smem_bytes() {
-    constexpr int TILE = RS_THREADS * RsItems<KB>::value;
+    constexpr int TILE = THREADS * RsItems<KB>::value;
     return (size_t)TILE * sizeof(KB) +
            (std::is_same<VB, NoValue>::value ? 0 : (size_t)TILE * sizeof(VB)) +
-           (size_t)RS_WARPS * RS_DIGITS * 4 * 2 + RS_DIGITS * 4 * 2 + 64;
+           (size_t)(THREADS / 32) * RS_DIGITS * 4 * 2 + RS_DIGITS * 4 * 2 + 64;
 }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
@@ -206,10 +206,11 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-template <typename KB, typename VB, typename W, int KIND, bool DESC>
-__global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
+template <typename KB, typename VB, typename W, int KIND, bool DESC, int THREADS>
+__global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(RsPass a) {
+    constexpr int RS_WARPS = THREADS / 32;
     constexpr int ITEMS = RsItems<KB>::value;
-    constexpr int TILE = RS_THREADS * ITEMS;
+    constexpr int TILE = THREADS * ITEMS;
     constexpr bool HAS_V = !std::is_same<VB, NoValue>::value;
     using F = LbFlags<W>;
 
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) s_misc[0] = atomicAdd(a.ticket, 1u);
-    for (int i = tid; i < RS_WARPS * RS_DIGITS; i += RS_THREADS) s_wc[i] = s_wm[i] = 0;
+    for (int i = tid; i < RS_WARPS * RS_DIGITS; i += THREADS) s_wc[i] = s_wm[i] = 0;
     __syncthreads();
     const uint64_t tile = s_misc[0];
     const uint64_t tile_base = tile * TILE;
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
             const char* src = reinterpret_cast<const char*>(vin + tile_base);
             char* dst = reinterpret_cast<char*>(s_vals);
 #pragma unroll
-            for (int c = tid; c < CHUNKS; c += RS_THREADS) cp_async16(dst + c * 16, src + c * 16);
+            for (int c = tid; c < CHUNKS; c += THREADS) cp_async16(dst + c * 16, src + c * 16);
             cp_async_commit();
         }
     }
@@ -402,7 +403,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) rs_onesweep_kernel(RsPass a) {
     VB* vout = reinterpret_cast<VB*>(a.vals_out);
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
-        const uint32_t idx = i * RS_THREADS + tid;
+        const uint32_t idx = i * THREADS + tid;
         if (idx < num_valid) {
             const KB k = s_keys[idx];
             const uint32_t d = digit_of<KB, KIND, DESC>(k, a.shift, a.mask);
@@ -423,11 +424,20 @@ struct RsLayout {
     size_t bins_off, ticket_off, lb_off, keys_off, vals_off, total, zero_bytes;
 };
 
+// CTA size of the onesweep kernel (tuning knob LCPP_RS_THREADS = 256 | 512).
+static int rs_threads() {
+    static const int t = [] {
+        const char* e = getenv("LCPP_RS_THREADS");
+        return (e && atoi(e) == 256) ? 256 : RS_THREADS;
+    }();
+    return t;
+}
+
 static RsLayout rs_layout(size_t ksize, size_t vsize, uint64_t n, uint32_t passes) {
     RsLayout L{};
     const int items = ksize == 4 ? RsItems<uint32_t>::value : RsItems<uint64_t>::value;
     L.passes = passes;
-    L.tiles = ceil_div(n ? n : 1, (uint64_t)RS_THREADS * items);
+    L.tiles = ceil_div(n ? n : 1, (uint64_t)rs_threads() * items);
     L.lb_word = n < (1ull << 30) ? 4 : 8;
     L.bins_off = 0;
     L.ticket_off = align_up(RS_MAX_PASSES * RS_DIGITS * 4, 256);
@@ -475,8 +485,10 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
         rs_bins_scan_kernel<<<L.passes, RS_DIGITS, 0, s>>>(bins); }
         count_launch(2);
     }
-    constexpr size_t smem = rs_smem_bytes<KB, VB>();
-    auto kern = rs_onesweep_kernel<KB, VB, W, KIND, DESC>;
+    const int threads = rs_threads();
+    const size_t smem = threads == 256 ? rs_smem_bytes<KB, VB, 256>() : rs_smem_bytes<KB, VB, RS_THREADS>();
+    auto kern = threads == 256 ? rs_onesweep_kernel<KB, VB, W, KIND, DESC, 256>
+                               : rs_onesweep_kernel<KB, VB, W, KIND, DESC, RS_THREADS>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return LCPP_ERR_CUDA;
 
@@ -502,7 +514,7 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
         a.lookback = lb + (size_t)p * L.tiles * RS_DIGITS * L.lb_word;
         a.ticket = tickets + p;
         { ProfScope ps("rs_onesweep", s);
-        kern<<<(unsigned)L.tiles, RS_THREADS, smem, s>>>(a); }
+        kern<<<(unsigned)L.tiles, threads, smem, s>>>(a); }
         count_launch();
         kcur = a.keys_out;
         vcur = a.vals_out;
