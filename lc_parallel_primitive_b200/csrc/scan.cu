@@ -43,7 +43,7 @@ template <> __device__ __forceinline__ int32_t from_bits<int32_t>(uint32_t b) { 
 template <typename T> __device__ __forceinline__ T add(T a, T b) { return OpSum::apply<T>(a, b); }
 
 __device__ __forceinline__ void backoff(uint32_t it) {
-    if (it > 4) __nanosleep(it < 64 ? 32 : 256);
+    if (it > 64) __nanosleep(it < 1024 ? 32 : 128);
 }
 
 // Warp-wide look-back over descriptors[0..tile): returns the sum of the
@@ -95,7 +95,7 @@ __device__ __forceinline__ T tile_prefix(uint64_t* desc, int64_t tile, T aggrega
 }
 
 template <typename T, bool INCLUSIVE>
-__global__ void __launch_bounds__(SCAN_THREADS, 2)
+__global__ void __launch_bounds__(SCAN_THREADS, 4)
 scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in,
             unsigned int* ticket, uint64_t* desc) {
     __shared__ unsigned int s_tile;
