@@ -4,11 +4,11 @@
 // (src/lcpp/device/details/single_pass_scan_operator.h:138-251).
 //
 // B200 design:
-//  * 8192-item tiles (512 threads x 16 items), 128-bit streaming loads and
+//  * 16384-item tiles (1024 threads x 16 items), 128-bit streaming loads and
 //    stores; each warp owns 512 contiguous items, each thread four 16-byte
 //    vectors at a 512-byte stride, so every load/store instruction is one
 //    fully coalesced 512-byte warp access.
-//  * Thread-local scans, then shuffle scans per vector, then a 16-entry scan of
+//  * Thread-local scans, then shuffle scans per vector, then a 32-entry scan of
 //    warp totals: no shared-memory transpose.
 //  * Tile descriptors are single 64-bit words {status:32 | value:32} written
 //    and read with relaxed device-scope atomics, so value and status can never
@@ -22,7 +22,7 @@
 
 namespace lcpp {
 
-constexpr int SCAN_THREADS = 512;
+constexpr int SCAN_THREADS = 1024;
 constexpr int SCAN_WARPS = SCAN_THREADS / 32;
 constexpr int SCAN_VECS = 4;                       // 16-byte vectors per thread
 constexpr int SCAN_ITEMS = SCAN_VECS * 4;          // 16 items (4-byte types)
@@ -95,7 +95,7 @@ __device__ __forceinline__ T tile_prefix(uint64_t* desc, int64_t tile, T aggrega
 }
 
 template <typename T, bool INCLUSIVE>
-__global__ void __launch_bounds__(SCAN_THREADS, 4)
+__global__ void __launch_bounds__(SCAN_THREADS, 2048 / SCAN_THREADS)
 scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in,
             unsigned int* ticket, uint64_t* desc) {
     __shared__ unsigned int s_tile;

@@ -25,7 +25,7 @@
 
 namespace lcpp {
 
-constexpr uint64_t SCAN_NOALLOC_MAX_TILES = 65536;  // n <= 65536 * 8192 = 2^29
+constexpr uint64_t SCAN_NOALLOC_MAX_TILES = (1ull << 29) / SCAN_TILE;  // n <= 2^29
 constexpr size_t SCAN_NOALLOC_BYTES = SCAN_HDR + SCAN_NOALLOC_MAX_TILES * sizeof(uint64_t);
 
 static __device__ __align__(256) unsigned char g_scan_noalloc_scratch[SCAN_NOALLOC_BYTES];
