@@ -24,7 +24,7 @@ namespace lcpp {
 
 constexpr int SCAN_THREADS = 1024;
 constexpr int SCAN_WARPS = SCAN_THREADS / 32;
-constexpr int SCAN_VECS = 4;                       // 16-byte vectors per thread
+constexpr int SCAN_VECS = 8;                       // 16-byte vectors per thread
 constexpr int SCAN_ITEMS = SCAN_VECS * 4;          // 16 items (4-byte types)
 constexpr int SCAN_WARP_ITEMS = 32 * SCAN_ITEMS;   // 512
 constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 8192
@@ -95,7 +95,7 @@ __device__ __forceinline__ T tile_prefix(uint64_t* desc, int64_t tile, T aggrega
 }
 
 template <typename T, bool INCLUSIVE>
-__global__ void __launch_bounds__(SCAN_THREADS, 2048 / SCAN_THREADS)
+__global__ void __launch_bounds__(SCAN_THREADS, 1)
 scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in,
             unsigned int* ticket, uint64_t* desc) {
     __shared__ unsigned int s_tile;
