@@ -3,6 +3,7 @@
 #include "runtime.cu"
 #include "reduce.cu"
 #include "scan.cu"
+#include "scan_pipe.cu"
 #include "radix_sort.cu"
 #include "segment_reduce.cu"
 #include "scan_noalloc.cu"

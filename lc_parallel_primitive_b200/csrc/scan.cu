@@ -29,6 +29,11 @@ constexpr int SCAN_ITEMS = SCAN_VECS * 4;          // 16 items (4-byte types)
 constexpr int SCAN_WARP_ITEMS = 32 * SCAN_ITEMS;   // 512
 constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 8192
 constexpr size_t SCAN_HDR = 256;                   // ticket counter + padding
+constexpr int SCAN_DESC_TILE = 8192;               // smallest tile of any scan kernel: sizes the descriptors
+
+template <typename T>
+static lcpp_status scan_pipe_launch(bool inclusive, const T* in, T* out, uint64_t n, const T* carry_in,
+                                    unsigned int* ticket, uint64_t* desc, cudaStream_t s);
 
 constexpr uint64_t ST_PARTIAL = 1ull << 32;
 constexpr uint64_t ST_INCLUSIVE = 2ull << 32;
@@ -224,7 +229,7 @@ using namespace lcpp;
 
 extern "C" size_t lcpp_scan_temp_bytes(int dtype, uint64_t n) {
     if (dtype != LCPP_I32 && dtype != LCPP_U32 && dtype != LCPP_F32) return 0;
-    const uint64_t tiles = ceil_div(n ? n : 1, SCAN_TILE);
+    const uint64_t tiles = ceil_div(n ? n : 1, SCAN_DESC_TILE);
     return SCAN_HDR + align_up(tiles * sizeof(uint64_t), 256);
 }
 
@@ -238,14 +243,20 @@ extern "C" lcpp_status lcpp_scan_carry(int kind, int dtype, const void* in, void
     if (n == 0) return LCPP_OK;
     if (!temp || temp_bytes < need) return LCPP_ERR_TEMP_TOO_SMALL;
     const uint64_t tiles = ceil_div(n, SCAN_TILE);
-    if (tiles > 0xffffffffull) return LCPP_ERR_INVALID_ARG;
+    const uint64_t desc_tiles = ceil_div(n, SCAN_DESC_TILE);
+    if (desc_tiles > 0xffffffffull) return LCPP_ERR_INVALID_ARG;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
     cudaStream_t s = (cudaStream_t)stream;
     unsigned int* ticket = (unsigned int*)temp;
     uint64_t* desc = (uint64_t*)((char*)temp + SCAN_HDR);
-    if (cudaMemsetAsync(temp, 0, SCAN_HDR + tiles * sizeof(uint64_t), s) != cudaSuccess) return LCPP_ERR_CUDA;
+    if (cudaMemsetAsync(temp, 0, SCAN_HDR + (aligned ? desc_tiles : tiles) * sizeof(uint64_t), s) != cudaSuccess)
+        return LCPP_ERR_CUDA;
     auto go = [&](auto zero) -> lcpp_status {
         using T = decltype(zero);
         ProfScope ps("scan", s);
+        if (aligned)  // pipelined persistent kernel (scan_pipe.cu)
+            return scan_pipe_launch<T>(kind == LCPP_SCAN_INCLUSIVE, (const T*)in, (T*)out, n, (const T*)carry_in,
+                                       ticket, desc, s);
         if (kind == LCPP_SCAN_INCLUSIVE)
             scan_kernel<T, true><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, (const T*)carry_in, ticket, desc);
         else

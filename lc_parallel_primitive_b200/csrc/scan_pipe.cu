@@ -1,0 +1,226 @@
+// Pipelined persistent DeviceScan kernel for 16-byte-aligned inputs.
+//
+// Same single-pass decoupled look-back as scan_kernel, reorganised so that
+// HBM never waits on the look-back:
+//  * persistent CTAs (2 per SM, 512 threads) stream 8192-item tiles through
+//    two 32 KiB shared-memory stages filled by TMA bulk copies
+//    (cp.async.bulk, this GPU's memory only, no multicast);
+//  * a CTA publishes the aggregate of its NEXT tile as soon as that tile's
+//    bulk load lands, before it resolves the look-back of its current tile.
+//    Partial descriptors therefore appear one tile ahead of the scan
+//    frontier, so a look-back never waits for another CTA's data to arrive
+//    (with one tile per CTA and no early publish, every look-back waits for
+//    the loads of all tiles in flight, which locks the CTAs into step);
+//  * results are written back into the stage and leave by bulk store.
+//
+// Forward progress: each CTA takes tile tickets in ascending order and
+// publishes a tile's aggregate depending only on that tile's own load; a
+// look-back waits only for aggregates of smaller tiles, which their CTAs
+// publish without waiting on anything else.  All waits are bounded.
+#include "bulk.cuh"
+#include "common.cuh"
+
+namespace lcpp {
+
+constexpr int SP_THREADS = 512;
+constexpr int SP_WARPS = SP_THREADS / 32;
+constexpr int SP_VECS = 4;
+constexpr int SP_WARP_ITEMS = 32 * SP_VECS * 4;  // 512
+constexpr int SP_TILE = SP_THREADS * SP_VECS * 4;  // 8192
+constexpr int SP_STAGE_BYTES = SP_TILE * 4;
+constexpr int SP_CTAS_PER_SM = 2;
+constexpr size_t SP_SMEM = 2 * (size_t)SP_STAGE_BYTES;
+static_assert(SP_TILE == SCAN_DESC_TILE, "descriptor array is sized for SCAN_DESC_TILE");
+
+template <typename T, bool INCLUSIVE>
+__global__ void __launch_bounds__(SP_THREADS, SP_CTAS_PER_SM)
+scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* carry_in,
+                 unsigned int* ticket, uint64_t* desc) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t s_bar[2];
+    __shared__ unsigned int s_tile[2];
+    __shared__ T s_agg[2];
+    __shared__ T s_warp[SP_WARPS];
+    __shared__ T s_wex[SP_WARPS];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint64_t full_tiles = n / SP_TILE;
+    const uint32_t limit = g_spin_limit;
+    const T c0 = carry_in ? *carry_in : T(0);
+    const uint32_t woff = (uint32_t)warp * SP_WARP_ITEMS + lane * 4;
+    uint32_t phase[2] = {0, 0};
+
+    auto issue = [&](unsigned int t, int st) {  // thread 0
+        if (t < full_tiles) {
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&s_bar[st], SP_STAGE_BYTES);
+            bulk_load(smem + st * SP_STAGE_BYTES, in + (uint64_t)t * SP_TILE, SP_STAGE_BYTES, &s_bar[st]);
+        }
+    };
+
+    // Make tile t's data available in stage st and publish its aggregate.
+    auto aggregate = [&](uint64_t t, int st) {
+        T* buf = reinterpret_cast<T*>(smem + st * SP_STAGE_BYTES);
+        if (t < full_tiles) {
+            if (!mbar_wait(&s_bar[st], phase[st], limit)) set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
+            phase[st] ^= 1;
+        } else {  // ragged last tile: guarded copy, zero fill
+            for (int i = tid; i < SP_TILE; i += SP_THREADS) {
+                const uint64_t g = t * SP_TILE + i;
+                buf[i] = g < n ? in[g] : T(0);
+            }
+            __syncthreads();
+        }
+        T s = T(0);
+#pragma unroll
+        for (int j = 0; j < SP_VECS; ++j) {
+            const uint4 q = *reinterpret_cast<const uint4*>(buf + woff + j * 128);
+            const T* e = reinterpret_cast<const T*>(&q);
+            s = add(s, add(add(e[0], e[1]), add(e[2], e[3])));
+        }
+        s = warp_reduce<OpSum>(s);
+        __syncthreads();  // earlier readers of s_warp are done
+        if (lane == 0) s_warp[warp] = s;
+        __syncthreads();
+        if (warp == 0) {
+            T a = lane < SP_WARPS ? s_warp[lane] : T(0);
+            a = warp_reduce<OpSum>(a);
+            if (lane == 0) {
+                s_agg[st] = a;
+                if (t == 0)
+                    st_relaxed_u64(desc, ST_INCLUSIVE | to_bits<T>(add(c0, a)));
+                else
+                    st_relaxed_u64(desc + t, ST_PARTIAL | to_bits<T>(a));
+            }
+        }
+    };
+
+    // Scan tile t held in stage st (its aggregate already published).
+    auto scan_tile = [&](uint64_t t, int st) {
+        T* buf = reinterpret_cast<T*>(smem + st * SP_STAGE_BYTES);
+        T x[SP_VECS][4];
+#pragma unroll
+        for (int j = 0; j < SP_VECS; ++j) {
+            const uint4 q = *reinterpret_cast<const uint4*>(buf + woff + j * 128);
+            const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) x[j][k] = e[k];
+        }
+        T pre[SP_VECS];
+        T carry = T(0);
+#pragma unroll
+        for (int j = 0; j < SP_VECS; ++j) {
+#pragma unroll
+            for (int k = 1; k < 4; ++k) x[j][k] = add(x[j][k - 1], x[j][k]);
+            T incl = x[j][3];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const T y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl = add(y, incl);
+            }
+            T excl = __shfl_up_sync(0xffffffffu, incl, 1);
+            if (lane == 0) excl = T(0);
+            pre[j] = add(carry, excl);
+            carry = add(carry, __shfl_sync(0xffffffffu, incl, 31));
+        }
+        __syncthreads();  // aggregate()'s readers of s_warp are done
+        if (lane == 0) s_warp[warp] = carry;
+        __syncthreads();
+        if (warp == 0) {
+            T incl = lane < SP_WARPS ? s_warp[lane] : T(0);
+#pragma unroll
+            for (int o = 1; o < SP_WARPS; o <<= 1) {
+                const T y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl = add(y, incl);
+            }
+            T wex = __shfl_up_sync(0xffffffffu, incl, 1);
+            if (lane == 0) wex = T(0);
+            T excl = c0;
+            if (t != 0) {
+                excl = lookback_warp<T>(desc, (int64_t)t);
+                if (lane == 0) st_relaxed_u64(desc + t, ST_INCLUSIVE | to_bits<T>(add(excl, s_agg[st])));
+            }
+            if (lane < SP_WARPS) s_wex[lane] = add(excl, wex);
+        }
+        __syncthreads();
+        const T wbase = s_wex[warp];
+        const bool full = t < full_tiles;
+#pragma unroll
+        for (int j = 0; j < SP_VECS; ++j) {
+            const T b = add(wbase, pre[j]);
+            T r[4];
+            if (INCLUSIVE) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) r[k] = add(b, x[j][k]);
+            } else {
+                r[0] = b;
+#pragma unroll
+                for (int k = 1; k < 4; ++k) r[k] = add(b, x[j][k - 1]);
+            }
+            if (full) {
+                *reinterpret_cast<uint4*>(buf + woff + j * 128) = *reinterpret_cast<const uint4*>(r);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint64_t g = t * SP_TILE + woff + j * 128 + k;
+                    if (g < n) out[g] = r[k];
+                }
+            }
+        }
+        if (full) fence_proxy_async_smem();
+        __syncthreads();
+        if (full && tid == 0) {
+            bulk_store(out + t * SP_TILE, buf, SP_STAGE_BYTES);
+            bulk_commit();
+        }
+    };
+
+    if (tid == 0) {
+        mbar_init(&s_bar[0], 1);
+        mbar_init(&s_bar[1], 1);
+        fence_mbar_init();
+        const unsigned int t0 = atomicAdd(ticket, 1u);
+        const unsigned int t1 = atomicAdd(ticket, 1u);
+        s_tile[0] = t0;
+        s_tile[1] = t1;
+        issue(t0, 0);
+        issue(t1, 1);
+    }
+    __syncthreads();
+
+    uint64_t c = s_tile[0];
+    int st = 0;
+    if (c < num_tiles) aggregate(c, 0);
+    while (c < num_tiles) {
+        const uint64_t nt = s_tile[st ^ 1];
+        if (nt < num_tiles) aggregate(nt, st ^ 1);
+        scan_tile(c, st);
+        if (tid == 0) {
+            const unsigned int nnt = atomicAdd(ticket, 1u);
+            s_tile[st] = nnt;
+            bulk_wait_read_all();  // this stage's bulk store has read it
+            issue(nnt, st);
+        }
+        __syncthreads();
+        c = nt;
+        st ^= 1;
+    }
+    if (tid == 0) bulk_wait_all();
+}
+
+template <typename T>
+static lcpp_status scan_pipe_launch(bool inclusive, const T* in, T* out, uint64_t n, const T* carry_in,
+                                    unsigned int* ticket, uint64_t* desc, cudaStream_t s) {
+    const uint64_t tiles = ceil_div(n, SP_TILE);
+    const DeviceInfo di = device_info();
+    uint64_t grid = (uint64_t)di.sms * SP_CTAS_PER_SM;
+    if (grid > ceil_div(tiles, 2)) grid = ceil_div(tiles, 2);
+    auto k = inclusive ? scan_pipe_kernel<T, true> : scan_pipe_kernel<T, false>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SP_SMEM) != cudaSuccess)
+        return LCPP_ERR_CUDA;
+    k<<<(unsigned)grid, SP_THREADS, SP_SMEM, s>>>(in, out, n, tiles, carry_in, ticket, desc);
+    count_launch();
+    return check_launch();
+}
+
+}  // namespace lcpp
