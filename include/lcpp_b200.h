@@ -136,7 +136,7 @@ lcpp_status lcpp_segment_reduce_fixed(int op, int dtype, const void* in, void* o
  * memory when they scan (allocator or memory-pool callbacks, plug-ins that
  * only receive their input/output buffers, real-time paths that forbid
  * allocation after start-up): same result as lcpp_scan, with the scratch
- * taken from a fixed ~512 KiB device array inside the library instead of a
+ * taken from a fixed ~128 KiB device array inside the library instead of a
  * caller temp buffer.  n <= lcpp_scan_noalloc_max_items() (2^29), larger n
  * returns LCPP_ERR_INVALID_ARG.  The array is shared by all calls on a device:
  * calls that overlap on the GPU race and must be serialized.  The first call

@@ -6,14 +6,14 @@
 // handed only pre-allocated input/output buffers by their host application,
 // and real-time paths that forbid allocation after start-up.  For them this
 // file keeps the scan's scratch (ticket counter + one 64-bit look-back
-// descriptor per 8192-item tile) in a fixed file-scope device array, so the
+// descriptor per tile) in a fixed file-scope device array, so the
 // call needs nothing but the input and output buffers.
 //
 // Limits and rules:
 //  * The array holds SCAN_NOALLOC_MAX_TILES descriptors: n <= 2^29 items
-//    (512 MiB of 4-byte data); larger n is rejected with
+//    (2 GiB of 4-byte data); larger n is rejected with
 //    LCPP_ERR_INVALID_ARG.  Every GPU that loads the library holds the
-//    array (~512 KiB) until the process exits.
+//    array (~128 KiB) until the process exits.
 //  * All calls on a device share the array.  Each call clears the part it
 //    uses before its kernel runs, but two calls that overlap on the GPU
 //    (different streams, no ordering between them) race on it: serialize

@@ -3,7 +3,7 @@
 // Same single-pass decoupled look-back as scan_kernel, reorganised so that
 // HBM never waits on the look-back:
 //  * persistent CTAs (2 per SM, 512 threads) stream 8192-item tiles through
-//    two 32 KiB shared-memory stages filled by TMA bulk copies
+//    three 32 KiB shared-memory stages filled by TMA bulk copies
 //    (cp.async.bulk, this GPU's memory only, no multicast);
 //  * a CTA publishes the aggregate of its NEXT tile as soon as that tile's
 //    bulk load lands, before it resolves the look-back of its current tile.
@@ -29,7 +29,8 @@ constexpr int SP_WARP_ITEMS = 32 * SP_VECS * 4;  // 512
 constexpr int SP_TILE = SP_THREADS * SP_VECS * 4;  // 8192
 constexpr int SP_STAGE_BYTES = SP_TILE * 4;
 constexpr int SP_CTAS_PER_SM = 2;
-constexpr size_t SP_SMEM = 2 * (size_t)SP_STAGE_BYTES;
+constexpr int SP_STAGES = 3;
+constexpr size_t SP_SMEM = SP_STAGES * (size_t)SP_STAGE_BYTES;
 static_assert(SP_TILE == SCAN_DESC_TILE, "descriptor array is sized for SCAN_DESC_TILE");
 
 template <typename T, bool INCLUSIVE>
@@ -37,9 +38,9 @@ __global__ void __launch_bounds__(SP_THREADS, SP_CTAS_PER_SM)
 scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* carry_in,
                  unsigned int* ticket, uint64_t* desc) {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t s_bar[2];
-    __shared__ unsigned int s_tile[2];
-    __shared__ T s_agg[2];
+    __shared__ __align__(8) uint64_t s_bar[SP_STAGES];
+    __shared__ unsigned int s_tile[SP_STAGES];
+    __shared__ T s_agg[SP_STAGES];
     __shared__ T s_warp[SP_WARPS];
     __shared__ T s_wex[SP_WARPS];
 
@@ -48,7 +49,7 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
     const uint32_t limit = g_spin_limit;
     const T c0 = carry_in ? *carry_in : T(0);
     const uint32_t woff = (uint32_t)warp * SP_WARP_ITEMS + lane * 4;
-    uint32_t phase[2] = {0, 0};
+    uint32_t phase[SP_STAGES] = {};
 
     auto issue = [&](unsigned int t, int st) {  // thread 0
         if (t < full_tiles) {
@@ -176,15 +177,13 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
     };
 
     if (tid == 0) {
-        mbar_init(&s_bar[0], 1);
-        mbar_init(&s_bar[1], 1);
+        for (int i = 0; i < SP_STAGES; ++i) mbar_init(&s_bar[i], 1);
         fence_mbar_init();
-        const unsigned int t0 = atomicAdd(ticket, 1u);
-        const unsigned int t1 = atomicAdd(ticket, 1u);
-        s_tile[0] = t0;
-        s_tile[1] = t1;
-        issue(t0, 0);
-        issue(t1, 1);
+        for (int i = 0; i < SP_STAGES; ++i) {
+            const unsigned int t = atomicAdd(ticket, 1u);
+            s_tile[i] = t;
+            issue(t, i);
+        }
     }
     __syncthreads();
 
@@ -192,8 +191,9 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
     int st = 0;
     if (c < num_tiles) aggregate(c, 0);
     while (c < num_tiles) {
-        const uint64_t nt = s_tile[st ^ 1];
-        if (nt < num_tiles) aggregate(nt, st ^ 1);
+        const int nst = st + 1 == SP_STAGES ? 0 : st + 1;
+        const uint64_t nt = s_tile[nst];
+        if (nt < num_tiles) aggregate(nt, nst);
         scan_tile(c, st);
         if (tid == 0) {
             const unsigned int nnt = atomicAdd(ticket, 1u);
@@ -203,7 +203,7 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
         }
         __syncthreads();
         c = nt;
-        st ^= 1;
+        st = nst;
     }
     if (tid == 0) bulk_wait_all();
 }
