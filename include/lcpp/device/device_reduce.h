@@ -1,0 +1,63 @@
+/*
+ * DeviceReduce — same class template, methods and argument meaning as the
+ * reference (src/lcpp/device/device_reduce.h:41-185); the work runs in the
+ * sm_100a kernels of liblcpp_b200.so through lcpp_reduce().
+ */
+#pragma once
+#include "lcpp/runtime/core.h"
+
+namespace luisa::parallel_primitive {
+
+template <size_t BLOCK_SIZE = details::BLOCK_SIZE, size_t WARP_NUMS = details::WARP_SIZE,
+          size_t ITEMS_PER_THREAD = details::ITEMS_PER_THREAD>
+class DeviceReduce : public LuisaModule {
+  public:
+    // Reference: device_reduce.h:68-78.  The debug stream, when given, makes
+    // every call commit and synchronize at once and assert success (debug
+    // builds), as lcpp_check does.
+    void create(Device& device, Stream* debug_stream = nullptr) {
+        m_device = device;
+        m_debug_stream = debug_stream;
+        m_created = true;
+    }
+
+    // Reference: device_reduce.h:84-91.
+    template <typename Type4Byte>
+    static size_t GetTempStorageBytes(size_t num_item) {
+        return lcpp_reduce_temp_bytes(lcpp_dtype_of<Type4Byte>(), num_item);
+    }
+
+    template <NumericT Type4Byte>
+    void Sum(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+             BufferView<Type4Byte> d_out, size_t num_item) {
+        record(cmdlist, LCPP_OP_SUM, temp_storage, d_in, d_out, num_item);
+    }
+    template <NumericT Type4Byte>
+    void Min(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+             BufferView<Type4Byte> d_out, size_t num_item) {
+        record(cmdlist, LCPP_OP_MIN, temp_storage, d_in, d_out, num_item);
+    }
+    // Starts from numeric_limits<T>::lowest() (the reference's min() at
+    // device_reduce.h:184 differs only for floating point).
+    template <NumericT Type4Byte>
+    void Max(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+             BufferView<Type4Byte> d_out, size_t num_item) {
+        record(cmdlist, LCPP_OP_MAX, temp_storage, d_in, d_out, num_item);
+    }
+
+  private:
+    template <typename T>
+    void record(CommandList& cmdlist, int op, BufferView<uint> temp, BufferView<T> in, BufferView<T> out,
+                size_t n) {
+        static_assert(lcpp_dtype_of<T>() >= 0, "unsupported element type");
+        cmdlist << [=](cudaStream_t s) {
+            return lcpp_reduce(op, lcpp_dtype_of<T>(), in.data(), out.data(), n, temp.data(), temp.size_bytes(), s);
+        };
+        lcpp_check(cmdlist, m_debug_stream);
+    }
+    Device m_device;
+    Stream* m_debug_stream = nullptr;
+    bool m_created = false;
+};
+
+}  // namespace luisa::parallel_primitive

@@ -1,0 +1,51 @@
+/*
+ * DeviceScan — same class template, methods and argument meaning as the
+ * reference (src/lcpp/device/device_scan.h:33-204); single-pass decoupled
+ * look-back scan in liblcpp_b200.so through lcpp_scan().  Element types: the
+ * reference's Type4Byte (int32, uint32, float).
+ */
+#pragma once
+#include "lcpp/runtime/core.h"
+
+namespace luisa::parallel_primitive {
+
+template <size_t BLOCK_SIZE = details::BLOCK_SIZE, size_t WARP_NUMS = details::WARP_SIZE,
+          size_t ITEMS_PER_THREAD = details::ITEMS_PER_THREAD>
+class DeviceScan : public LuisaModule {
+  public:
+    void create(Device& device, Stream* debug_stream = nullptr) {  // device_scan.h:59-69
+        m_device = device;
+        m_debug_stream = debug_stream;
+    }
+
+    template <typename Type4Byte>
+    static size_t GetTempStorageBytes(size_t num_items) {  // device_scan.h:75-89
+        return lcpp_scan_temp_bytes(lcpp_dtype_of<Type4Byte>(), num_items);
+    }
+
+    template <NumericT Type4Byte>
+    void ExclusiveSum(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+                      BufferView<Type4Byte> d_out, size_t num_items) {
+        record(cmdlist, LCPP_SCAN_EXCLUSIVE, temp_storage, d_in, d_out, num_items);
+    }
+    template <NumericT Type4Byte>
+    void InclusiveSum(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+                      BufferView<Type4Byte> d_out, size_t num_items) {
+        record(cmdlist, LCPP_SCAN_INCLUSIVE, temp_storage, d_in, d_out, num_items);
+    }
+
+  private:
+    template <typename T>
+    void record(CommandList& cmdlist, int kind, BufferView<uint> temp, BufferView<T> in, BufferView<T> out,
+                size_t n) {
+        static_assert(sizeof(T) == 4, "DeviceScan serves 4-byte types");
+        cmdlist << [=](cudaStream_t s) {
+            return lcpp_scan(kind, lcpp_dtype_of<T>(), in.data(), out.data(), n, temp.data(), temp.size_bytes(), s);
+        };
+        lcpp_check(cmdlist, m_debug_stream);
+    }
+    Device m_device;
+    Stream* m_debug_stream = nullptr;
+};
+
+}  // namespace luisa::parallel_primitive

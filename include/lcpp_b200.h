@@ -117,7 +117,11 @@ lcpp_status lcpp_radix_sort(int key_dtype, int value_dtype, int descending,
  * (device_segment_reduce.h:125-194; Max's init is lowest(), :186-194).
  * dtype: any of I32 U32 F32 I64 U64 F64.  Offsets are uint32 (the
  * reference's BufferView<uint>); a CSR offsets[S+1] array is passed as
- * begin = offsets, end = offsets + 1. */
+ * begin = offsets, end = offsets + 1.  temp may be NULL or smaller than
+ * lcpp_segment_reduce_temp_bytes(): the call then reduces every segment with
+ * one warp (the reference's GetTempStorageBytes returns 0 here,
+ * device_segment_reduce.h:71-75); with the full temp, segments longer than
+ * 4096 items go to whole CTAs. */
 size_t      lcpp_segment_reduce_temp_bytes(int dtype, uint64_t num_items,
                                            uint64_t num_segments);
 lcpp_status lcpp_segment_reduce(int op, int dtype, const void* in, void* out,

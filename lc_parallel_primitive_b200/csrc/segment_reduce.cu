@@ -44,7 +44,7 @@ seg_warp_kernel(const T* __restrict__ in, T* __restrict__ out, uint64_t num_segm
         e = __ldg(end + s);
         if (e < b) e = b;
     }
-    if (e - b > SEG_LONG) {
+    if (long_list && e - b > SEG_LONG) {
         if (lane == 0) long_list[atomicAdd(long_count, 1u)] = (uint32_t)s;
         return;
     }
@@ -139,6 +139,13 @@ static lcpp_status seg_launch(const void* in, void* out, uint64_t S, const uint3
         count_launch();
         return check_launch();
     }
+    if (!temp) {  // no work list: every segment is reduced by one warp
+        ProfScope ps("seg_warp", s);
+        seg_warp_kernel<Op, T, false><<<(unsigned)ceil_div(S, SEG_A_WARPS), SEG_A_THREADS, 0, s>>>(
+            (const T*)in, (T*)out, S, begin, end, 0, init, nullptr, nullptr);
+        count_launch();
+        return check_launch();
+    }
     unsigned int* cnt = (unsigned int*)temp;
     uint32_t* list = (uint32_t*)((char*)temp + SEG_HDR);
     if (cudaMemsetAsync(cnt, 0, sizeof(unsigned int), s) != cudaSuccess) return LCPP_ERR_CUDA;
@@ -180,8 +187,9 @@ extern "C" lcpp_status lcpp_segment_reduce(int op, int dtype, const void* in, vo
     if (op < 0 || op > 2 || !lcpp_dtype_size(dtype)) return LCPP_ERR_INVALID_ARG;
     if (num_segments == 0) return LCPP_OK;
     if (!out || !begin_offsets || !end_offsets || num_segments > 0xffffffffull) return LCPP_ERR_INVALID_ARG;
-    if (!temp || temp_bytes < lcpp_segment_reduce_temp_bytes(dtype, 0, num_segments))
-        return LCPP_ERR_TEMP_TOO_SMALL;
+    // Without enough temp for the long-segment work list the call still runs:
+    // one warp per segment, long ones included (slower on very long segments).
+    if (!temp || temp_bytes < lcpp_segment_reduce_temp_bytes(dtype, 0, num_segments)) temp = nullptr;
     return dispatch_dtype(dtype, [&](auto zero) -> lcpp_status {
         using T = decltype(zero);
         return seg_op<T>(op, in, out, num_segments, begin_offsets, end_offsets, 0, false, temp,

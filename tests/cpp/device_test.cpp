@@ -1,0 +1,225 @@
+// C++ drop-in test: the reference's own device tests (tests/device_reduce_test.cpp,
+// device_scan_test.cpp, device_radix_sort_one_sweep.cpp, device_segment_reduce.cpp),
+// restated against the B200 build's public headers with the same inputs,
+// seeds and std:: expectations.  Exit code 0 = all checks passed.
+#include <lcpp/parallel_primitive.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <functional>
+#include <numeric>
+#include <random>
+
+using namespace luisa;
+using namespace luisa::compute;
+using namespace luisa::parallel_primitive;
+
+static int g_failures = 0;
+#define EXPECT(cond, ...)                                  \
+    do {                                                   \
+        if (!(cond)) {                                     \
+            ++g_failures;                                  \
+            std::printf("FAIL %s:%d ", __FILE__, __LINE__); \
+            std::printf(__VA_ARGS__);                      \
+            std::printf("\n");                             \
+        }                                                  \
+    } while (0)
+
+int main(int argc, char* argv[]) {
+    Context context{argv[0]};
+    Device device = context.create_device("cuda");
+    Stream stream = device.create_stream();
+
+    // ---- device_reduce_test.cpp:66-90 / 118-166 --------------------------------
+    {
+        DeviceReduce<> reducer;
+        reducer.create(device, &stream);
+        for (uint loop = 0; loop < 24; ++loop) {
+            uint n = (1u << loop) + 1;
+            auto d_in = device.create_buffer<uint>(n);
+            auto d_out = device.create_buffer<uint>(1);
+            std::vector<uint> host(n, 1);
+            stream << d_in.copy_from(host.data()) << synchronize();
+            size_t tb = DeviceReduce<>::GetTempStorageBytes<uint>(n);
+            auto temp = device.create_buffer<uint>(bytes_to_uint_count(tb));
+            CommandList cmdlist;
+            reducer.Sum(cmdlist, temp.view(), d_in.view(), d_out.view(), n);
+            stream << cmdlist.commit() << synchronize();
+            std::vector<uint> out(1);
+            stream << d_out.copy_to(out.data()) << synchronize();
+            EXPECT(out[0] == n, "reduce ones n=%u got %u", n, out[0]);
+        }
+        const int N = 1 << 12;
+        std::vector<int32> input(N);
+        std::iota(input.begin(), input.end(), 0);
+        std::mt19937 rng(114521);
+        std::shuffle(input.begin(), input.end(), rng);
+        auto d_in = device.create_buffer<int32>(N);
+        auto d_out = device.create_buffer<int32>(1);
+        stream << d_in.copy_from(input.data()) << synchronize();
+        auto temp = device.create_buffer<uint>(bytes_to_uint_count(DeviceReduce<>::GetTempStorageBytes<int32>(N)));
+        std::vector<int32> r(1);
+        CommandList cmdlist;
+        reducer.Min(cmdlist, temp.view(), d_in.view(), d_out.view(), d_in.size());
+        stream << cmdlist.commit() << synchronize() << d_out.copy_to(r.data()) << synchronize();
+        EXPECT(r[0] == *std::min_element(input.begin(), input.end()), "reduce min %d", r[0]);
+        reducer.Max(cmdlist, temp.view(), d_in.view(), d_out.view(), d_in.size());
+        stream << cmdlist.commit() << synchronize() << d_out.copy_to(r.data()) << synchronize();
+        EXPECT(r[0] == *std::max_element(input.begin(), input.end()), "reduce max %d", r[0]);
+    }
+
+    // ---- device_scan_test.cpp:67-108 ------------------------------------------
+    {
+        using ScannerT = DeviceScan<256, 32, 4>;
+        ScannerT scanner;
+        scanner.create(device, &stream);
+        CommandList cmdlist;
+        for (int i = 0; i < 24; i++) {
+            const uint n = 1u << i;
+            std::vector<uint> input(n, 1);
+            auto in = device.create_buffer<uint>(n);
+            auto ex = device.create_buffer<uint>(n);
+            auto inc = device.create_buffer<uint>(n);
+            stream << in.copy_from(input.data()) << synchronize();
+            auto temp = device.create_buffer<uint>(bytes_to_uint_count(ScannerT::GetTempStorageBytes<uint>(n)));
+            scanner.ExclusiveSum(cmdlist, temp.view(), in.view(), ex.view(), in.size());
+            stream << cmdlist.commit() << synchronize();
+            scanner.InclusiveSum(cmdlist, temp.view(), in.view(), inc.view(), in.size());
+            stream << cmdlist.commit() << synchronize();
+            std::vector<uint> er(n), ir(n), ee(n), ie(n);
+            stream << ex.copy_to(er.data()) << inc.copy_to(ir.data()) << synchronize();
+            std::exclusive_scan(input.begin(), input.end(), ee.begin(), 0u);
+            std::inclusive_scan(input.begin(), input.end(), ie.begin());
+            EXPECT(er == ee && ir == ie, "scan failed for size 2^%d", i);
+        }
+    }
+
+    // ---- device_radix_sort_one_sweep.cpp:61-151, 153-279 -----------------------
+    {
+        using SorterT = DeviceRadixSort<128, 32, 4>;
+        SorterT sorter;
+        sorter.create(device, &stream);
+        CommandList cmdlist;
+        for (uint loop = 5; loop < 25; ++loop) {
+            uint n = 1u << loop;
+            std::vector<float> a(n), d(n);
+            std::mt19937 rng(114521);
+            std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+            for (uint i = 0; i < n; i++) { a[i] = dist(rng); d[i] = dist(rng); }
+            auto ain = device.create_buffer<float>(n), aout = device.create_buffer<float>(n);
+            auto din = device.create_buffer<float>(n), dout = device.create_buffer<float>(n);
+            stream << ain.copy_from(a.data()) << din.copy_from(d.data()) << synchronize();
+            auto temp = device.create_buffer<uint>(bytes_to_uint_count(SorterT::GetSortKeysTempStorageBytes<float>(n)));
+            sorter.SortKeys<float>(cmdlist, temp.view(), ain.view(), aout.view(), ain.size());
+            sorter.SortKeysDescending<float>(cmdlist, temp.view(), din.view(), dout.view(), din.size());
+            stream << cmdlist.commit() << synchronize();
+            std::vector<float> ar(n), dr(n);
+            stream << aout.copy_to(ar.data()) << dout.copy_to(dr.data()) << synchronize();
+            std::sort(a.begin(), a.end());
+            std::sort(d.begin(), d.end(), std::greater<float>());
+            EXPECT(ar == a, "float asc n=%u", n);
+            EXPECT(dr == d, "float desc n=%u", n);
+        }
+        DeviceRadixSort<> s2;
+        s2.create(device, &stream);
+        for (uint loop = 0; loop < 24; ++loop) {
+            uint n = 1u << loop;
+            std::vector<uint> keys(n);
+            for (uint i = 0; i < n; ++i) keys[i] = n - i - 1;
+            auto kin = device.create_buffer<uint>(n), kout = device.create_buffer<uint>(n);
+            stream << kin.copy_from(keys.data()) << synchronize();
+            auto temp = device.create_buffer<uint>(bytes_to_uint_count(DeviceRadixSort<>::GetSortKeysTempStorageBytes<uint>(n)));
+            CommandList cl;
+            s2.SortKeys(cl, temp.view(), kin.view(), kout.view(), n);
+            stream << cl.commit() << synchronize();
+            std::vector<uint> r(n);
+            stream << kout.copy_to(r.data()) << synchronize();
+            std::sort(keys.begin(), keys.end());
+            EXPECT(r == keys, "uint reversed n=%u", n);
+        }
+        const int N = 524288;
+        std::vector<uint> k(N), dk(N);
+        std::vector<float> v(N), dv(N);
+        std::mt19937 rng(114521);
+        std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+        for (int i = 0; i < N; i++) { k[i] = i; dk[i] = i; }
+        std::shuffle(k.begin(), k.end(), rng);
+        std::shuffle(dk.begin(), dk.end(), rng);
+        for (int i = 0; i < N; i++) { v[i] = dist(rng); dv[i] = dist(rng); }
+        std::vector<std::pair<uint, float>> p(N), dp(N);
+        for (int i = 0; i < N; i++) { p[i] = {k[i], v[i]}; dp[i] = {dk[i], dv[i]}; }
+        auto kb = device.create_buffer<uint>(N), ko = device.create_buffer<uint>(N);
+        auto vb = device.create_buffer<float>(N), vo = device.create_buffer<float>(N);
+        auto dkb = device.create_buffer<uint>(N), dko = device.create_buffer<uint>(N);
+        auto dvb = device.create_buffer<float>(N), dvo = device.create_buffer<float>(N);
+        stream << kb.copy_from(k.data()) << vb.copy_from(v.data()) << dkb.copy_from(dk.data())
+               << dvb.copy_from(dv.data()) << synchronize();
+        auto temp = device.create_buffer<uint>(bytes_to_uint_count(SorterT::GetSortPairsTempStorageBytes<uint, float>(N)));
+        sorter.SortPairs<uint, float>(cmdlist, temp.view(), kb.view(), ko.view(), vb.view(), vo.view(), kb.size());
+        stream << cmdlist.commit() << synchronize();
+        sorter.SortPairsDescending<uint, float>(cmdlist, temp.view(), dkb.view(), dko.view(), dvb.view(), dvo.view(),
+                                                dkb.size());
+        stream << cmdlist.commit() << synchronize();
+        std::vector<uint> rk(N), rdk(N);
+        std::vector<float> rv(N), rdv(N);
+        stream << ko.copy_to(rk.data()) << vo.copy_to(rv.data()) << dko.copy_to(rdk.data())
+               << dvo.copy_to(rdv.data()) << synchronize();
+        std::sort(p.begin(), p.end(), [](auto& a, auto& b) { return a.first < b.first; });
+        std::sort(dp.begin(), dp.end(), [](auto& a, auto& b) { return a.first > b.first; });
+        bool ok = true, dok = true;
+        for (int i = 0; i < N; i++) {
+            ok &= rk[i] == p[i].first && rv[i] == p[i].second;
+            dok &= rdk[i] == dp[i].first && rdv[i] == dp[i].second;
+        }
+        EXPECT(ok, "pairs ascending");
+        EXPECT(dok, "pairs descending");
+    }
+
+    // ---- device_segment_reduce.cpp:62-176 --------------------------------------
+    {
+        DeviceSegmentReduce<> reducer;
+        reducer.create(device, &stream);
+        CommandList cmdlist;
+        const int N = 1024, per = 100;
+        std::vector<int32> input(N);
+        std::iota(input.begin(), input.end(), 0);
+        std::mt19937 rng(114521);
+        std::shuffle(input.begin(), input.end(), rng);
+        const int S = N / per + 1;
+        std::vector<uint> b(S), e(S);
+        for (int i = 0; i < N; i++)
+            if (i % per == 0) { b[i / per] = i; e[i / per] = std::min(i + per, N); }
+        auto in = device.create_buffer<int32>(N);
+        auto out = device.create_buffer<int32>(S);
+        auto bb = device.create_buffer<uint>(S), eb = device.create_buffer<uint>(S);
+        stream << in.copy_from(input.data()) << bb.copy_from(b.data()) << eb.copy_from(e.data()) << synchronize();
+        auto temp = device.create_buffer<uint>(
+            std::max<size_t>(1, bytes_to_uint_count(DeviceSegmentReduce<>::GetTempStorageBytes<int32>(N))));
+        reducer.Sum(cmdlist, temp.view(), in.view(), out.view(), S, bb.view(), eb.view());
+        stream << cmdlist.commit() << synchronize();
+        std::vector<int32> r(S);
+        stream << out.copy_to(r.data()) << synchronize();
+        for (int s = 0; s < S; s++) {
+            int want = std::accumulate(input.begin() + b[s], input.begin() + e[s], 0);
+            EXPECT(r[s] == want, "segment %d got %d want %d", s, r[s], want);
+        }
+        // fixed size: 32 segments of 32 over iota(1024)
+        std::vector<int32> iota(N);
+        std::iota(iota.begin(), iota.end(), 0);
+        auto in2 = device.create_buffer<int32>(N);
+        auto out2 = device.create_buffer<int32>(32);
+        stream << in2.copy_from(iota.data()) << synchronize();
+        reducer.Sum(cmdlist, temp.view(), in2.view(), out2.view(), 32u, 32u);
+        stream << cmdlist.commit() << synchronize();
+        std::vector<int32> r2(32);
+        stream << out2.copy_to(r2.data()) << synchronize();
+        for (int s = 0; s < 32; s++) {
+            int want = std::accumulate(iota.begin() + s * 32, iota.begin() + (s + 1) * 32, 0);
+            EXPECT(r2[s] == want, "fixed segment %d", s);
+        }
+    }
+
+    EXPECT(stream.last_status() == 0, "stream status %d", stream.last_status());
+    std::printf("%s: %d failure(s)\n", g_failures ? "FAILED" : "OK", g_failures);
+    return g_failures ? 1 : 0;
+}

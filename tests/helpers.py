@@ -112,7 +112,7 @@ def abi_sort(keys_np, values_np=None, descending=False, begin_bit=0, end_bit=0, 
     return to_host(ko), to_host(vo)
 
 
-def abi_segment_reduce(op, x_np, begin_np, end_np):
+def abi_segment_reduce(op, x_np, begin_np, end_np, with_temp=True):
     import torch
 
     lib = L.lib()
@@ -122,10 +122,10 @@ def abi_segment_reduce(op, x_np, begin_np, end_np):
     e = to_dev(end_np.astype(np.uint32))
     S = begin_np.size
     out = empty_dev(S, x_np.dtype)
-    tb = lib.lcpp_segment_reduce_temp_bytes(dt, x_np.size, S)
-    t = temp(tb)
+    tb = lib.lcpp_segment_reduce_temp_bytes(dt, x_np.size, S) if with_temp else 0
+    t = temp(tb) if with_temp else None
     L.check(lib.lcpp_segment_reduce(op, dt, d.data_ptr(), out.data_ptr(), S, b.data_ptr(), e.data_ptr(),
-                                    t.data_ptr(), tb, stream()))
+                                    None if t is None else t.data_ptr(), tb, stream()))
     torch.cuda.synchronize()
     L.check(lib.lcpp_last_device_error(stream()))
     return to_host(out)

@@ -79,6 +79,16 @@ def test_long_and_empty_segments(cuda):
     assert np.array_equal(abi_segment_reduce(2, xi, b, e), oracle.segment_reduce(2, xi, b, e))
 
 
+def test_without_temp_storage(cuda):
+    # temp = NULL: every segment (long ones too) is reduced by one warp.
+    lens = np.array([0, 3, 5000, 0, 70000, 1, 4096, 4097], dtype=np.uint64)
+    off = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+    b, e = off[:-1], off[1:]
+    xi = G.u32(int(off[-1]), seed=8).view(np.int32)
+    for op in (0, 1, 2):
+        assert np.array_equal(abi_segment_reduce(op, xi, b, e, with_temp=False), oracle.segment_reduce(op, xi, b, e))
+
+
 def test_fixed_size_paths(cuda):
     for seg, S in ((1, 1000), (32, 1000), (100, 777), (4096, 50), (5000, 40), (70000, 3)):
         x = G.u32(seg * S, seed=seg).view(np.int32)
