@@ -1,0 +1,222 @@
+"""Multi-GPU primitives on one node: one process per GPU, torch.distributed
+(NCCL over NVLink/NVSwitch) for the exchange steps, this library's sm_100a
+kernels (C ABI) for every local pass.  The reference has no multi-GPU support;
+these follow the partitioning of its single-GPU semantics:
+
+* mg_reduce          contiguous shards -> local DeviceReduce -> all_reduce of
+                     one element per rank.
+* mg_scan            contiguous shards -> local reduce -> all_gather of the G
+                     shard totals -> carry = sum of the totals of lower ranks
+                     -> local single-pass scan seeded with the carry
+                     (12 bytes of HBM traffic per element).  Bit-exact for
+                     integers (sums wrap mod 2^32 like the single-GPU scan).
+* mg_sort_pairs      global stable sort of the concatenation of the shards in
+                     rank order: local onesweep sort -> regular samples of the
+                     sorted shard all-gathered -> G-1 splitters -> each rank
+                     cuts its sorted shard at the splitters (all keys equal to
+                     a splitter go to the same rank) -> all_to_all of keys and
+                     values -> final local onesweep sort of the received runs
+                     (stable, and runs arrive in source-rank order, so equal
+                     keys keep their global input order).  Rank r ends up with
+                     the r-th slice of the global order; slices are contiguous
+                     and ordered but not equal in size.
+
+Local work goes through an ``ops`` object: ``GpuOps`` (the default) calls the
+CUDA kernels and fails loudly without them.  Tests of the host logic on CPU
+ranks (gloo) pass a CPU implementation explicitly; the library never falls
+back to one.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+from .primitives import lcpp_dtype
+
+# ---------------------------------------------------------------------------
+# Local operations on one GPU (C ABI)
+# ---------------------------------------------------------------------------
+
+
+class GpuOps:
+    """Local passes on the current CUDA device through liblcpp_b200.so."""
+
+    def __init__(self, stream=None):
+        self.lib = L.lib()
+        self.stream = stream
+
+    def _s(self):
+        return (self.stream or torch.cuda.current_stream()).cuda_stream
+
+    @staticmethod
+    def _tmp(nbytes, device):
+        return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+    def reduce(self, op: int, x: torch.Tensor) -> torch.Tensor:
+        dt = lcpp_dtype(x)
+        out = torch.empty(1, dtype=x.dtype, device=x.device)
+        tb = self.lib.lcpp_reduce_temp_bytes(dt, x.numel())
+        t = self._tmp(tb, x.device)
+        L.check(self.lib.lcpp_reduce(op, dt, x.data_ptr(), out.data_ptr(), x.numel(), t.data_ptr(), tb, self._s()),
+                "mg reduce")
+        return out
+
+    def scan(self, inclusive: bool, x: torch.Tensor, out: torch.Tensor, carry: torch.Tensor | None) -> None:
+        dt = lcpp_dtype(x)
+        tb = self.lib.lcpp_scan_temp_bytes(dt, x.numel())
+        t = self._tmp(tb, x.device)
+        L.check(self.lib.lcpp_scan_carry(int(inclusive), dt, x.data_ptr(), out.data_ptr(), x.numel(),
+                                         None if carry is None else carry.data_ptr(), t.data_ptr(), tb, self._s()),
+                "mg scan")
+
+    def sort_pairs(self, keys: torch.Tensor, vals: torch.Tensor, temp: torch.Tensor | None = None):
+        kd, vd = lcpp_dtype(keys), lcpp_dtype(vals)
+        n = keys.numel()
+        ko, vo = torch.empty_like(keys), torch.empty_like(vals)
+        if n == 0:
+            return ko, vo
+        tb = self.lib.lcpp_radix_sort_temp_bytes(kd, vd, n)
+        t = temp if temp is not None and temp.numel() >= tb else self._tmp(tb, keys.device)
+        L.check(self.lib.lcpp_radix_sort(kd, vd, 0, keys.data_ptr(), ko.data_ptr(), vals.data_ptr(), vo.data_ptr(),
+                                         n, 0, 0, t.data_ptr(), tb, self._s()), "mg sort")
+        return ko, vo
+
+
+# ---------------------------------------------------------------------------
+# Order-preserving signed 64-bit image of keys (for splitters/searchsorted)
+# ---------------------------------------------------------------------------
+_SIGN64 = -(1 << 63)
+
+
+def ordered_i64(keys: torch.Tensor) -> torch.Tensor:
+    """int64 tensor whose signed order equals the keys' sort order (unsigned
+    keys: flip the top bit of the 64-bit image; signed: widen)."""
+    if keys.dtype in (torch.int32, torch.int64):
+        return keys.to(torch.int64)
+    if keys.dtype == torch.uint32:
+        return keys.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    if keys.dtype == torch.uint64:
+        return keys.view(torch.int64) ^ _SIGN64
+    raise TypeError(f"mg_sort_pairs: unsupported key type {keys.dtype}")
+
+
+def _all_gather_1d(x: torch.Tensor, group=None) -> torch.Tensor:
+    """Concatenation of every rank's equally sized 1-D tensor, in rank order."""
+    world = dist.get_world_size(group)
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x.contiguous(), group=group)
+    return torch.cat(parts)
+
+
+def _op_to_reduce_op(op: int):
+    return {L.OP_SUM: dist.ReduceOp.SUM, L.OP_MIN: dist.ReduceOp.MIN, L.OP_MAX: dist.ReduceOp.MAX}[op]
+
+
+# ---------------------------------------------------------------------------
+def mg_reduce(op: int, x_local: torch.Tensor, ops=None, group=None) -> torch.Tensor:
+    """Reduction of the concatenation of all ranks' shards (result on every rank)."""
+    ops = ops or GpuOps()
+    part = ops.reduce(op, x_local)
+    if part.dtype == torch.uint32:  # collectives on 32-bit unsigned: sum wraps identically on int32 bits;
+        if op == L.OP_SUM:         # min/max compare on the zero-extended int64 image
+            p = part.view(torch.int32).clone()
+            dist.all_reduce(p, op=dist.ReduceOp.SUM, group=group)
+            return p.view(torch.uint32)
+        p = part.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+        dist.all_reduce(p, op=_op_to_reduce_op(op), group=group)
+        return p.to(torch.int32).view(torch.uint32)
+    p = part.clone()
+    dist.all_reduce(p, op=_op_to_reduce_op(op), group=group)
+    return p
+
+
+def shard_carry(totals: torch.Tensor, rank: int) -> torch.Tensor:
+    """Exclusive sum of the shard totals of ranks below `rank` (wrapping for
+    32-bit integers), as a 1-element tensor of the totals' dtype."""
+    if totals.dtype in (torch.int32, torch.uint32):
+        t = totals.view(torch.int32).to(torch.int64)[:rank].sum() & 0xFFFFFFFF
+        c = t.to(torch.int64).reshape(1)
+        c = torch.where(c >= (1 << 31), c - (1 << 32), c).to(torch.int32)
+        return c.view(totals.dtype)
+    return totals[:rank].sum().reshape(1).to(totals.dtype)
+
+
+def mg_scan(inclusive: bool, x_local: torch.Tensor, out_local: torch.Tensor, ops=None, group=None) -> None:
+    """Prefix sum of the concatenation of all ranks' shards, in rank order."""
+    ops = ops or GpuOps()
+    rank = dist.get_rank(group)
+    total = ops.reduce(L.OP_SUM, x_local)
+    if total.dtype == torch.uint32:
+        gathered = _all_gather_1d(total.view(torch.int32), group).view(torch.uint32)
+    else:
+        gathered = _all_gather_1d(total, group)
+    carry = shard_carry(gathered, rank)
+    ops.scan(inclusive, x_local, out_local, carry if rank > 0 else None)
+
+
+@dataclass
+class SortResult:
+    keys: torch.Tensor
+    values: torch.Tensor
+    counts_per_rank: list  # number of elements that ended on each rank (all_gathered)
+
+
+def choose_splitters(samples_sorted_i64: torch.Tensor, world: int) -> torch.Tensor:
+    """G-1 splitters from the globally sorted sample: every (len/G)-th sample."""
+    m = samples_sorted_i64.numel()
+    if world == 1 or m == 0:
+        return samples_sorted_i64.new_empty(0)
+    idx = torch.arange(1, world, device=samples_sorted_i64.device) * m // world
+    return samples_sorted_i64[idx]
+
+
+def split_counts(sorted_keys_i64: torch.Tensor, splitters: torch.Tensor) -> torch.Tensor:
+    """Elements of a sorted shard that go to each rank: rank r receives keys
+    in [splitter[r-1], splitter[r]) (first rank from -inf, last to +inf)."""
+    n = sorted_keys_i64.numel()
+    cuts = torch.searchsorted(sorted_keys_i64, splitters, right=False) if splitters.numel() else \
+        splitters.new_empty(0)
+    bounds = torch.cat([cuts.new_zeros(1), cuts, cuts.new_full((1,), n)])
+    return (bounds[1:] - bounds[:-1]).to(torch.int64)
+
+
+def mg_sort_pairs(keys_local: torch.Tensor, vals_local: torch.Tensor, ops=None, group=None,
+                  samples_per_rank: int = 1024) -> SortResult:
+    """Globally stable sort of (keys, values) sharded over the ranks in rank
+    order.  Returns this rank's slice of the sorted sequence."""
+    ops = ops or GpuOps()
+    world = dist.get_world_size(group)
+    k1, v1 = ops.sort_pairs(keys_local, vals_local)  # local onesweep
+    if world == 1:
+        return SortResult(k1, v1, [k1.numel()])
+    dev = k1.device
+    ki = ordered_i64(k1)
+    n = ki.numel()
+    s = min(samples_per_rank, max(n, 1))
+    if n:
+        pos = (torch.arange(s, device=dev, dtype=torch.int64) * n) // s
+        samp = ki[pos]
+    else:
+        samp = torch.full((s,), torch.iinfo(torch.int64).max, dtype=torch.int64, device=dev)
+    all_samp, _ = torch.sort(_all_gather_1d(samp, group))  # G*s samples: tiny
+    splitters = choose_splitters(all_samp, world)
+    send_counts = split_counts(ki, splitters)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    sc = send_counts.cpu().tolist()
+    rc = recv_counts.cpu().tolist()
+    nrecv = int(sum(rc))
+    # keys and values move as raw bits (int32/int64 views for NCCL)
+    kview = torch.int64 if k1.element_size() == 8 else torch.int32
+    vview = torch.int64 if v1.element_size() == 8 else torch.int32
+    rk = torch.empty(nrecv, dtype=kview, device=dev)
+    rv = torch.empty(nrecv, dtype=vview, device=dev)
+    dist.all_to_all_single(rk, k1.view(kview), output_split_sizes=rc, input_split_sizes=sc, group=group)
+    dist.all_to_all_single(rv, v1.view(vview), output_split_sizes=rc, input_split_sizes=sc, group=group)
+    del k1, v1, ki
+    k2, v2 = ops.sort_pairs(rk.view(keys_local.dtype), rv.view(vals_local.dtype))  # final local pass
+    all_counts = _all_gather_1d(torch.tensor([nrecv], dtype=torch.int64, device=dev), group)
+    return SortResult(k2, v2, all_counts.cpu().tolist())
