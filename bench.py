@@ -200,7 +200,8 @@ def main():
     n = 1 << args.n_log2
     keys_np = G.u32(n, seed=1 + rank, stream=7)
     h_keys = torch.from_numpy(keys_np.view(np.int32)).pin_memory()
-    h_vals = torch.from_numpy(G.iota_u32(n).view(np.int32)).pin_memory()
+    # values = global input index (shard r holds elements r*n .. r*n+n-1)
+    h_vals = torch.from_numpy(G.iota_u32(n, start=(rank * n) & 0xFFFFFFFF).view(np.int32)).pin_memory()
     h_keys_out = torch.empty_like(h_keys).pin_memory()
     h_vals_out = torch.empty_like(h_vals).pin_memory()
     d_keys = h_keys.to(dev)
@@ -210,9 +211,18 @@ def main():
     tb = lib.lcpp_radix_sort_temp_bytes(L.U32, L.U32, n)
     d_temp = torch.empty(tb, dtype=torch.uint8, device=dev)
 
+    mg_state = {}
+
     def sort_once():
-        L.check(lib.lcpp_radix_sort(L.U32, L.U32, 0, d_keys.data_ptr(), d_keys_out.data_ptr(), d_vals.data_ptr(),
-                                    d_vals_out.data_ptr(), n, 0, 0, d_temp.data_ptr(), tb, sh), "sort")
+        if world == 1:
+            L.check(lib.lcpp_radix_sort(L.U32, L.U32, 0, d_keys.data_ptr(), d_keys_out.data_ptr(),
+                                        d_vals.data_ptr(), d_vals_out.data_ptr(), n, 0, 0, d_temp.data_ptr(), tb,
+                                        sh), "sort")
+        else:  # global sort across the ranks: local sort, splitters, all-to-all, final local sort
+            from lc_parallel_primitive_b200.multi_gpu import mg_sort_pairs
+
+            r = mg_sort_pairs(d_keys.view(torch.uint32), d_vals.view(torch.uint32))
+            mg_state["res"] = r
 
     for _ in range(args.warmup):
         sort_once()
@@ -220,11 +230,25 @@ def main():
     L.check(lib.lcpp_last_device_error(sh), "device error")
 
     # correctness of what is timed (size-independent properties on the device)
-    k = d_keys_out.view(torch.int32) ^ torch.tensor(-(1 << 31), dtype=torch.int32, device=dev)
-    assert bool((k[1:] >= k[:-1]).all()), "sort output not ordered"
-    perm_keys = d_keys.view(torch.int32)[d_vals_out.view(torch.int32).long()]
-    assert bool((perm_keys == d_keys_out.view(torch.int32)).all()), "values do not follow keys"
-    del k, perm_keys
+    if world == 1:
+        k = d_keys_out.view(torch.int32) ^ torch.tensor(-(1 << 31), dtype=torch.int32, device=dev)
+        assert bool((k[1:] >= k[:-1]).all()), "sort output not ordered"
+        perm_keys = d_keys.view(torch.int32)[d_vals_out.view(torch.int32).long()]
+        assert bool((perm_keys == d_keys_out.view(torch.int32)).all()), "values do not follow keys"
+        del k, perm_keys
+    else:
+        r = mg_state["res"]
+        k = r.keys.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+        assert bool((k[1:] >= k[:-1]).all()), "rank slice not ordered"
+        ends = torch.tensor([k[0].item() if k.numel() else -1, k[-1].item() if k.numel() else -1],
+                            dtype=torch.int64, device=dev)
+        allends = [torch.empty_like(ends) for _ in range(world)]
+        torch.distributed.all_gather(allends, ends)
+        e = torch.stack(allends).cpu().tolist()
+        assert all(e[i][1] <= e[i + 1][0] for i in range(world - 1) if e[i][1] >= 0 and e[i + 1][0] >= 0)
+        assert sum(r.counts_per_rank) == world * n
+        del k
+        mg_state.clear()
     torch.cuda.empty_cache()
 
     def barrier():
@@ -298,8 +322,9 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u32", "data": "synthetic (PCG32 seeded, uniform u32 keys, iota values)",
-            "config": {"workload": f"DeviceRadixSort::SortPairs, n=2^{args.n_log2} u32 keys + u32 values per GPU (BASELINE config 3)",
-                       "n_per_gpu": n, "parallelism": f"independent shards x{world}" if world > 1 else "single GPU",
+            "config": {"workload": f"DeviceRadixSort::SortPairs, n=2^{args.n_log2} u32 keys + u32 values per GPU (BASELINE config 3)"
+                       + ("" if world == 1 else "; global sort over all GPUs (local onesweep, sampled splitters, NCCL all-to-all, final onesweep)"),
+                       "n_per_gpu": n, "parallelism": f"global sort x{world} (torch.distributed NCCL all_to_all)" if world > 1 else "single GPU",
                        "l2": "inputs 2 GiB per step > 126 MB L2 (no flush needed)",
                        "algorithmic_bytes_per_pair": 68},
             "roofline": {"bound": "hbm", "kernel": "rs_onesweep_kernel (one 8-bit pass)",
@@ -340,22 +365,35 @@ def run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_k
     barrier()
     torch.cuda.synchronize()
     e0.record(stream)
+    d2h = 0
     for _ in range(e2e_steps):
         d_keys.copy_(h_keys, non_blocking=True)
         d_vals.copy_(h_vals, non_blocking=True)
-        cmd = CommandList()
-        sorter.SortPairs(cmd, d_temp, d_keys, d_keys_out, d_vals, d_vals_out, n)
-        api_stream << cmd.commit()
-        h_keys_out.copy_(d_keys_out, non_blocking=True)
-        h_vals_out.copy_(d_vals_out, non_blocking=True)
+        if world == 1:
+            cmd = CommandList()
+            sorter.SortPairs(cmd, d_temp, d_keys, d_keys_out, d_vals, d_vals_out, n)
+            api_stream << cmd.commit()
+            h_keys_out.copy_(d_keys_out, non_blocking=True)
+            h_vals_out.copy_(d_vals_out, non_blocking=True)
+            d2h = 8 * n
+        else:  # the multi-GPU entry point; this rank's slice of the result comes back
+            from lc_parallel_primitive_b200.multi_gpu import mg_sort_pairs
+
+            r = mg_sort_pairs(d_keys.view(torch.uint32), d_vals.view(torch.uint32))
+            m = min(r.keys.numel(), h_keys_out.numel())
+            h_keys_out[:m].copy_(r.keys.view(torch.int32)[:m], non_blocking=True)
+            h_vals_out[:m].copy_(r.values.view(torch.int32)[:m], non_blocking=True)
+            d2h = 8 * r.keys.numel()
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    assert np.array_equal(h_vals_out[:1000].numpy(), d_vals_out[:1000].cpu().numpy())
+    if world == 1:
+        assert np.array_equal(h_vals_out[:1000].numpy(), d_vals_out[:1000].cpu().numpy())
     return {"value": world * n / (e2e_ms * 1e-3) / 1e9, "unit": UNIT, "h2d_bytes_per_step": 8 * n,
-            "d2h_bytes_per_step": 8 * n, "ms_per_step": e2e_ms,
-            "api": "DeviceRadixSort.SortPairs via CommandList/Stream", "steps": e2e_steps}
+            "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+            "api": "DeviceRadixSort.SortPairs via CommandList/Stream" if world == 1 else "multi_gpu.mg_sort_pairs",
+            "steps": e2e_steps}
 
 
 def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier, shrink=0):
