@@ -11,14 +11,17 @@ these follow the partitioning of its single-GPU semantics:
                      (12 bytes of HBM traffic per element).  Bit-exact for
                      integers (sums wrap mod 2^32 like the single-GPU scan).
 * mg_sort_pairs      global stable sort of the concatenation of the shards in
-                     rank order: local onesweep sort -> regular samples of the
-                     sorted shard all-gathered -> G-1 splitters -> each rank
-                     cuts its sorted shard at the splitters (all keys equal to
-                     a splitter go to the same rank) -> all_to_all of keys and
-                     values -> final local onesweep sort of the received runs
-                     (stable, and runs arrive in source-rank order, so equal
-                     keys keep their global input order).  Rank r ends up with
-                     the r-th slice of the global order; slices are contiguous
+                     rank order: one stable onesweep pass on the top 8 key
+                     bits partitions each shard into 256 buckets -> the
+                     all-reduced bucket counts assign contiguous bucket
+                     ranges to ranks -> all_to_all of keys and values ->
+                     full local onesweep sort of the received runs (stable,
+                     and runs arrive in source-rank order, so equal keys keep
+                     their global input order).  When the buckets cannot be
+                     split evenly (skewed keys) each shard is fully sorted and
+                     cut at sampled splitters instead (all keys equal to a
+                     splitter go to the same rank).  Rank r ends up with the
+                     r-th slice of the global order; slices are contiguous
                      and ordered but not equal in size.
 
 Local work goes through an ``ops`` object: ``GpuOps`` (the default) calls the
@@ -72,7 +75,8 @@ class GpuOps:
                                          None if carry is None else carry.data_ptr(), t.data_ptr(), tb, self._s()),
                 "mg scan")
 
-    def sort_pairs(self, keys: torch.Tensor, vals: torch.Tensor, temp: torch.Tensor | None = None):
+    def sort_pairs(self, keys: torch.Tensor, vals: torch.Tensor, temp: torch.Tensor | None = None,
+                   begin_bit: int = 0, end_bit: int = 0):
         kd, vd = lcpp_dtype(keys), lcpp_dtype(vals)
         n = keys.numel()
         ko, vo = torch.empty_like(keys), torch.empty_like(vals)
@@ -81,7 +85,7 @@ class GpuOps:
         tb = self.lib.lcpp_radix_sort_temp_bytes(kd, vd, n)
         t = temp if temp is not None and temp.numel() >= tb else self._tmp(tb, keys.device)
         L.check(self.lib.lcpp_radix_sort(kd, vd, 0, keys.data_ptr(), ko.data_ptr(), vals.data_ptr(), vo.data_ptr(),
-                                         n, 0, 0, t.data_ptr(), tb, self._s()), "mg sort")
+                                         n, begin_bit, end_bit, t.data_ptr(), tb, self._s()), "mg sort")
         return ko, vo
 
 
@@ -183,27 +187,45 @@ def split_counts(sorted_keys_i64: torch.Tensor, splitters: torch.Tensor) -> torc
     return (bounds[1:] - bounds[:-1]).to(torch.int64)
 
 
-def mg_sort_pairs(keys_local: torch.Tensor, vals_local: torch.Tensor, ops=None, group=None,
-                  samples_per_rank: int = 1024) -> SortResult:
-    """Globally stable sort of (keys, values) sharded over the ranks in rank
-    order.  Returns this rank's slice of the sorted sequence."""
-    ops = ops or GpuOps()
-    world = dist.get_world_size(group)
-    k1, v1 = ops.sort_pairs(keys_local, vals_local)  # local onesweep
-    if world == 1:
-        return SortResult(k1, v1, [k1.numel()])
-    dev = k1.device
-    ki = ordered_i64(k1)
-    n = ki.numel()
-    s = min(samples_per_rank, max(n, 1))
-    if n:
-        pos = (torch.arange(s, device=dev, dtype=torch.int64) * n) // s
-        samp = ki[pos]
-    else:
-        samp = torch.full((s,), torch.iinfo(torch.int64).max, dtype=torch.int64, device=dev)
-    all_samp, _ = torch.sort(_all_gather_1d(samp, group))  # G*s samples: tiny
-    splitters = choose_splitters(all_samp, world)
-    send_counts = split_counts(ki, splitters)
+def bucket_lower_bounds(dtype, device) -> torch.Tensor:
+    """ordered_i64 value at which each of the 256 top-byte buckets of the
+    key's order-preserving image starts."""
+    b = torch.arange(256, dtype=torch.int64, device=device)
+    if dtype == torch.uint32:
+        return b << 24
+    if dtype == torch.int32:
+        return (b - 128) << 24
+    if dtype in (torch.uint64, torch.int64):
+        return (b - 128) << 56
+    raise TypeError(f"mg_sort_pairs: unsupported key type {dtype}")
+
+
+def rank_bucket_ranges(global_counts: list, world: int):
+    """Split the 256 top-byte buckets into `world` contiguous ranges of about
+    equal element count.  Returns (bucket boundaries[world+1], max load / mean load)."""
+    total = sum(global_counts)
+    cum, acc = [], 0
+    for c in global_counts:
+        acc += c
+        cum.append(acc)
+    bounds = [0]
+    for r in range(1, world):
+        target = total * r / world
+        # first bucket whose end overshoots the target starts rank r, unless
+        # stopping before it is closer to the target
+        b = next((i for i, e in enumerate(cum) if e > target), 256)
+        before = cum[b - 1] if b > 0 else 0
+        if b < 256 and cum[b] - target < target - before:
+            b += 1
+        bounds.append(max(b, bounds[-1]))
+    bounds.append(256)
+    loads = [(cum[bounds[r + 1] - 1] if bounds[r + 1] > 0 else 0) - (cum[bounds[r] - 1] if bounds[r] > 0 else 0)
+             for r in range(world)]
+    mean = total / world if world else 0
+    return bounds, (max(loads) / mean if mean else 1.0)
+
+
+def _exchange(k1, v1, send_counts, keys_dtype, vals_dtype, group):
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
     sc = send_counts.cpu().tolist()
@@ -212,11 +234,56 @@ def mg_sort_pairs(keys_local: torch.Tensor, vals_local: torch.Tensor, ops=None, 
     # keys and values move as raw bits (int32/int64 views for NCCL)
     kview = torch.int64 if k1.element_size() == 8 else torch.int32
     vview = torch.int64 if v1.element_size() == 8 else torch.int32
-    rk = torch.empty(nrecv, dtype=kview, device=dev)
-    rv = torch.empty(nrecv, dtype=vview, device=dev)
+    rk = torch.empty(nrecv, dtype=kview, device=k1.device)
+    rv = torch.empty(nrecv, dtype=vview, device=k1.device)
     dist.all_to_all_single(rk, k1.view(kview), output_split_sizes=rc, input_split_sizes=sc, group=group)
     dist.all_to_all_single(rv, v1.view(vview), output_split_sizes=rc, input_split_sizes=sc, group=group)
-    del k1, v1, ki
-    k2, v2 = ops.sort_pairs(rk.view(keys_local.dtype), rv.view(vals_local.dtype))  # final local pass
-    all_counts = _all_gather_1d(torch.tensor([nrecv], dtype=torch.int64, device=dev), group)
+    return rk.view(keys_dtype), rv.view(vals_dtype)
+
+
+def mg_sort_pairs(keys_local: torch.Tensor, vals_local: torch.Tensor, ops=None, group=None,
+                  samples_per_rank: int = 1024, max_imbalance: float = 1.25) -> SortResult:
+    """Globally stable sort of (keys, values) sharded over the ranks in rank
+    order.  Returns this rank's slice of the sorted sequence.
+
+    Fast path: one stable onesweep pass on the top 8 key bits partitions the
+    shard; an all-reduced 256-bin count assigns contiguous bucket ranges to
+    ranks; if that split is balanced (max load <= max_imbalance x mean) the
+    buckets are exchanged and each rank sorts what it received.  Otherwise
+    (skewed keys) the shard is fully sorted and cut at sampled splitters.
+    """
+    ops = ops or GpuOps()
+    world = dist.get_world_size(group)
+    if world == 1:
+        k1, v1 = ops.sort_pairs(keys_local, vals_local)
+        return SortResult(k1, v1, [k1.numel()])
+    dev = keys_local.device
+    kbits = keys_local.element_size() * 8
+    k1, v1 = ops.sort_pairs(keys_local, vals_local, begin_bit=kbits - 8, end_bit=kbits)  # partition pass
+    ki = ordered_i64(k1)
+    n = ki.numel()
+    cut = torch.searchsorted(ki, bucket_lower_bounds(keys_local.dtype, dev))
+    local_counts = torch.diff(torch.cat([cut, cut.new_full((1,), n)]))
+    global_counts = local_counts.clone()
+    dist.all_reduce(global_counts, group=group)
+    bounds, imbalance = rank_bucket_ranges(global_counts.cpu().tolist(), world)
+    if imbalance <= max_imbalance:
+        starts = torch.cat([cut, cut.new_full((1,), n)])[torch.tensor(bounds, device=dev)]
+        send_counts = torch.diff(starts).to(torch.int64)
+        del ki
+    else:
+        k1, v1 = ops.sort_pairs(k1, v1)  # full local sort (stable: partition kept input order)
+        ki = ordered_i64(k1)
+        s = min(samples_per_rank, max(n, 1))
+        if n:
+            samp = ki[(torch.arange(s, device=dev, dtype=torch.int64) * n) // s]
+        else:
+            samp = torch.full((s,), torch.iinfo(torch.int64).max, dtype=torch.int64, device=dev)
+        all_samp, _ = torch.sort(_all_gather_1d(samp, group))  # G*s samples: tiny
+        send_counts = split_counts(ki, choose_splitters(all_samp, world))
+        del ki
+    rk, rv = _exchange(k1, v1, send_counts, keys_local.dtype, vals_local.dtype, group)
+    del k1, v1
+    k2, v2 = ops.sort_pairs(rk, rv)  # final local sort of the received runs
+    all_counts = _all_gather_1d(torch.tensor([rk.numel()], dtype=torch.int64, device=dev), group)
     return SortResult(k2, v2, all_counts.cpu().tolist())

@@ -28,6 +28,6 @@ class CpuOps:
             y = (y + c).astype(y.dtype) if x.dtype != torch.float32 else (y + np.float32(c)).astype(np.float32)
         out.copy_(torch.from_numpy(np.ascontiguousarray(y)))
 
-    def sort_pairs(self, keys, vals):
-        k, v = oracle.radix_sort(_np(keys), _np(vals))
+    def sort_pairs(self, keys, vals, begin_bit=0, end_bit=0):
+        k, v = oracle.radix_sort(_np(keys), _np(vals), begin_bit=begin_bit, end_bit=end_bit)
         return torch.from_numpy(k), torch.from_numpy(v)

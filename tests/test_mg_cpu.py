@@ -37,13 +37,15 @@ def _worker(rank, world, port, q):
         bounds = [N * r // world for r in range(world + 1)]
         lo, hi = bounds[rank], bounds[rank + 1]
         res = M.mg_sort_pairs(torch.from_numpy(keys[lo:hi].copy()), torch.from_numpy(vals[lo:hi].copy()), ops=ops)
+        ukeys = rng.integers(0, 1 << 32, size=N, dtype=np.uint64).astype(np.uint32)  # balanced: bucket path
+        ures = M.mg_sort_pairs(torch.from_numpy(ukeys[lo:hi].copy()), torch.from_numpy(vals[lo:hi].copy()), ops=ops)
         xs = rng.integers(0, 1 << 32, size=N, dtype=np.uint64).astype(np.uint32)
         out = torch.empty(hi - lo, dtype=torch.uint32)
         M.mg_scan(False, torch.from_numpy(xs[lo:hi].copy()), out, ops=ops)
         red = M.mg_reduce(L.OP_MAX, torch.from_numpy(xs[lo:hi].copy()), ops=ops)
         tot = M.mg_reduce(L.OP_SUM, torch.from_numpy(xs[lo:hi].copy()), ops=ops)
         q.put((rank, res.keys.numpy(), res.values.numpy(), res.counts_per_rank, out.numpy(), int(red[0]),
-               int(tot.view(torch.int32)[0]) & 0xFFFFFFFF))
+               int(tot.view(torch.int32)[0]) & 0xFFFFFFFF, ures.keys.numpy(), ures.values.numpy()))
     finally:
         dist.destroy_process_group()
 
@@ -64,7 +66,11 @@ def test_mg_host_logic_on_cpu_ranks(world):
     N = 10007
     keys = rng.integers(0, 50, size=N, dtype=np.uint32)
     vals = np.arange(N, dtype=np.uint32)
+    ukeys = rng.integers(0, 1 << 32, size=N, dtype=np.uint64).astype(np.uint32)
     xs = rng.integers(0, 1 << 32, size=N, dtype=np.uint64).astype(np.uint32)
+    uo = np.argsort(ukeys, kind="stable")
+    assert np.array_equal(np.concatenate([g[7] for g in got]), ukeys[uo])
+    assert np.array_equal(np.concatenate([g[8] for g in got]), vals[uo])
     order = np.argsort(keys, kind="stable")
     k = np.concatenate([g[1] for g in got])
     v = np.concatenate([g[2] for g in got])
