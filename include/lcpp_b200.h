@@ -111,6 +111,16 @@ lcpp_status lcpp_radix_sort(int key_dtype, int value_dtype, int descending,
                             int begin_bit, int end_bit,
                             void* temp, size_t temp_bytes, void* stream);
 
+/* Boundaries of the 256 digit runs of keys that are already ordered by the
+ * 8-bit digit at bit_start (e.g. after lcpp_radix_sort with
+ * begin_bit = bit_start, end_bit = bit_start + 8): starts[d] = first index
+ * whose digit is >= d, starts[256] = n (257 uint64 outputs, device memory).
+ * Digits use the same order-preserving key image as the sort (ascending).
+ * No counterpart in the reference; the multi-GPU sort uses it to cut a
+ * partitioned shard into per-rank bucket ranges. */
+lcpp_status lcpp_radix_bucket_starts(int key_dtype, const void* keys, uint64_t n, int bit_start,
+                                     uint64_t* starts, void* stream);
+
 /* ---- DeviceSegmentReduce ------------------------------------------------
  * out[s] = init (+) reduce(in[begin[s]..end[s])); empty segment -> init.
  * Replaces DeviceSegmentReduce::Sum/Min/Max with begin/end offset views

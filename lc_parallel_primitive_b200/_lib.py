@@ -42,6 +42,7 @@ SIGNATURES = {
     "lcpp_scan_noalloc": (_i, [_i, _i, _vp, _vp, _u64, _vp]),
     "lcpp_radix_sort_temp_bytes": (_sz, [_i, _i, _u64]),
     "lcpp_radix_sort": (_i, [_i, _i, _i, _vp, _vp, _vp, _vp, _u64, _i, _i, _vp, _sz, _vp]),
+    "lcpp_radix_bucket_starts": (_i, [_i, _vp, _u64, _i, _vp, _vp]),
     "lcpp_segment_reduce_temp_bytes": (_sz, [_i, _u64, _u64]),
     "lcpp_segment_reduce": (_i, [_i, _i, _vp, _vp, _u64, _vp, _vp, _vp, _sz, _vp]),
     "lcpp_segment_reduce_fixed": (_i, [_i, _i, _vp, _vp, _u64, _u64, _vp]),

@@ -595,3 +595,43 @@ extern "C" lcpp_status lcpp_radix_sort(int key_dtype, int value_dtype, int desce
     if (vs == 4) return rs_dispatch_kind<uint64_t, uint32_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
     return rs_dispatch_kind<uint64_t, uint64_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
 }
+
+// ---------------------------------------------------------------------------
+// Digit-run boundaries of keys already ordered by one 8-bit digit.
+// ---------------------------------------------------------------------------
+namespace lcpp {
+
+template <typename KB, int KIND>
+__global__ void rs_bucket_starts_kernel(const KB* keys, uint64_t n, uint32_t shift, uint64_t* starts) {
+    const uint32_t b = threadIdx.x;  // 256 threads: first index whose digit >= b
+    uint64_t lo = 0, hi = n;
+    while (lo < hi) {
+        const uint64_t mid = (lo + hi) >> 1;
+        const uint32_t d = (uint32_t)(ordered_bits<KB, KIND, false>(keys[mid]) >> shift) & 0xFFu;
+        if (d < b) lo = mid + 1; else hi = mid;
+    }
+    starts[b] = lo;
+    if (b == 0) starts[RS_DIGITS] = n;
+}
+
+}  // namespace lcpp
+
+extern "C" lcpp_status lcpp_radix_bucket_starts(int key_dtype, const void* keys, uint64_t n, int bit_start,
+                                                uint64_t* starts, void* stream) {
+    const int kind = key_kind(key_dtype);
+    const int kbits = (int)lcpp_dtype_size(key_dtype) * 8;
+    if (kind < 0 || !starts || (n && !keys) || bit_start < 0 || bit_start + 8 > kbits) return LCPP_ERR_INVALID_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    auto go = [&](auto kb) -> lcpp_status {
+        using KB = decltype(kb);
+        const KB* k = (const KB*)keys;
+        switch (kind) {
+            case 0: rs_bucket_starts_kernel<KB, 0><<<1, RS_DIGITS, 0, s>>>(k, n, bit_start, starts); break;
+            case 1: rs_bucket_starts_kernel<KB, 1><<<1, RS_DIGITS, 0, s>>>(k, n, bit_start, starts); break;
+            default: rs_bucket_starts_kernel<KB, 2><<<1, RS_DIGITS, 0, s>>>(k, n, bit_start, starts); break;
+        }
+        count_launch();
+        return check_launch();
+    };
+    return kbits == 32 ? go((uint32_t)0) : go((uint64_t)0);
+}

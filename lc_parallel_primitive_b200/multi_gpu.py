@@ -75,6 +75,13 @@ class GpuOps:
                                          None if carry is None else carry.data_ptr(), t.data_ptr(), tb, self._s()),
                 "mg scan")
 
+    def bucket_starts(self, keys: torch.Tensor, bit_start: int) -> torch.Tensor:
+        """257 run boundaries of keys ordered by the 8-bit digit at bit_start."""
+        out = torch.empty(257, dtype=torch.int64, device=keys.device)
+        L.check(self.lib.lcpp_radix_bucket_starts(lcpp_dtype(keys), keys.data_ptr(), keys.numel(), bit_start,
+                                                  out.data_ptr(), self._s()), "mg bucket starts")
+        return out
+
     def sort_pairs(self, keys: torch.Tensor, vals: torch.Tensor, temp: torch.Tensor | None = None,
                    begin_bit: int = 0, end_bit: int = 0):
         kd, vd = lcpp_dtype(keys), lcpp_dtype(vals)
@@ -187,19 +194,6 @@ def split_counts(sorted_keys_i64: torch.Tensor, splitters: torch.Tensor) -> torc
     return (bounds[1:] - bounds[:-1]).to(torch.int64)
 
 
-def bucket_lower_bounds(dtype, device) -> torch.Tensor:
-    """ordered_i64 value at which each of the 256 top-byte buckets of the
-    key's order-preserving image starts."""
-    b = torch.arange(256, dtype=torch.int64, device=device)
-    if dtype == torch.uint32:
-        return b << 24
-    if dtype == torch.int32:
-        return (b - 128) << 24
-    if dtype in (torch.uint64, torch.int64):
-        return (b - 128) << 56
-    raise TypeError(f"mg_sort_pairs: unsupported key type {dtype}")
-
-
 def rank_bucket_ranges(global_counts: list, world: int):
     """Split the 256 top-byte buckets into `world` contiguous ranges of about
     equal element count.  Returns (bucket boundaries[world+1], max load / mean load)."""
@@ -226,18 +220,41 @@ def rank_bucket_ranges(global_counts: list, world: int):
 
 
 def _exchange(k1, v1, send_counts, keys_dtype, vals_dtype, group):
+    """Send send_counts[r] consecutive (key, value) pairs to rank r; receive
+    the runs of every rank, concatenated in source-rank order.  Keys and
+    values travel as raw bits in one batch of NCCL point-to-point calls."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
     sc = send_counts.cpu().tolist()
     rc = recv_counts.cpu().tolist()
-    nrecv = int(sum(rc))
-    # keys and values move as raw bits (int32/int64 views for NCCL)
     kview = torch.int64 if k1.element_size() == 8 else torch.int32
     vview = torch.int64 if v1.element_size() == 8 else torch.int32
-    rk = torch.empty(nrecv, dtype=kview, device=k1.device)
-    rv = torch.empty(nrecv, dtype=vview, device=k1.device)
-    dist.all_to_all_single(rk, k1.view(kview), output_split_sizes=rc, input_split_sizes=sc, group=group)
-    dist.all_to_all_single(rv, v1.view(vview), output_split_sizes=rc, input_split_sizes=sc, group=group)
+    rk = torch.empty(int(sum(rc)), dtype=kview, device=k1.device)
+    rv = torch.empty(int(sum(rc)), dtype=vview, device=k1.device)
+    ks, vs = k1.view(kview), v1.view(vview)
+    so, ro = [0], [0]
+    for c in sc:
+        so.append(so[-1] + c)
+    for c in rc:
+        ro.append(ro[-1] + c)
+    p2p = []
+    for p in range(world):
+        if p == rank:
+            continue
+        peer = dist.get_global_rank(group, p) if group is not None else p
+        if sc[p]:
+            p2p.append(dist.P2POp(dist.isend, ks[so[p]:so[p + 1]], peer, group))
+            p2p.append(dist.P2POp(dist.isend, vs[so[p]:so[p + 1]], peer, group))
+        if rc[p]:
+            p2p.append(dist.P2POp(dist.irecv, rk[ro[p]:ro[p + 1]], peer, group))
+            p2p.append(dist.P2POp(dist.irecv, rv[ro[p]:ro[p + 1]], peer, group))
+    rk[ro[rank]:ro[rank + 1]].copy_(ks[so[rank]:so[rank + 1]])
+    rv[ro[rank]:ro[rank + 1]].copy_(vs[so[rank]:so[rank + 1]])
+    if p2p:
+        for w in dist.batch_isend_irecv(p2p):
+            w.wait()
     return rk.view(keys_dtype), rv.view(vals_dtype)
 
 
@@ -260,17 +277,13 @@ def mg_sort_pairs(keys_local: torch.Tensor, vals_local: torch.Tensor, ops=None, 
     dev = keys_local.device
     kbits = keys_local.element_size() * 8
     k1, v1 = ops.sort_pairs(keys_local, vals_local, begin_bit=kbits - 8, end_bit=kbits)  # partition pass
-    ki = ordered_i64(k1)
-    n = ki.numel()
-    cut = torch.searchsorted(ki, bucket_lower_bounds(keys_local.dtype, dev))
-    local_counts = torch.diff(torch.cat([cut, cut.new_full((1,), n)]))
-    global_counts = local_counts.clone()
+    n = k1.numel()
+    starts = ops.bucket_starts(k1, kbits - 8)  # 257 run boundaries
+    global_counts = torch.diff(starts)
     dist.all_reduce(global_counts, group=group)
     bounds, imbalance = rank_bucket_ranges(global_counts.cpu().tolist(), world)
     if imbalance <= max_imbalance:
-        starts = torch.cat([cut, cut.new_full((1,), n)])[torch.tensor(bounds, device=dev)]
-        send_counts = torch.diff(starts).to(torch.int64)
-        del ki
+        send_counts = torch.diff(starts[torch.tensor(bounds, device=dev)]).to(torch.int64)
     else:
         k1, v1 = ops.sort_pairs(k1, v1)  # full local sort (stable: partition kept input order)
         ki = ordered_i64(k1)

@@ -28,6 +28,13 @@ class CpuOps:
             y = (y + c).astype(y.dtype) if x.dtype != torch.float32 else (y + np.float32(c)).astype(np.float32)
         out.copy_(torch.from_numpy(np.ascontiguousarray(y)))
 
+    def bucket_starts(self, keys, bit_start):
+        k = _np(keys).astype(np.uint64)
+        if keys.dtype in (torch.int32, torch.int64):
+            k = (_np(keys).astype(np.int64) + (1 << (keys.element_size() * 8 - 1))).astype(np.uint64)
+        d = (k >> np.uint64(bit_start)) & np.uint64(0xFF)
+        return torch.from_numpy(np.searchsorted(d, np.arange(257, dtype=np.uint64), side="left").astype(np.int64))
+
     def sort_pairs(self, keys, vals, begin_bit=0, end_bit=0):
         k, v = oracle.radix_sort(_np(keys), _np(vals), begin_bit=begin_bit, end_bit=end_bit)
         return torch.from_numpy(k), torch.from_numpy(v)
