@@ -39,7 +39,7 @@ METRIC = "Onesweep sort Gkeys/s; scan/reduce HBM GB/s (% of ~8 TB/s) at 1/2/4/8 
 UNIT = "Gkeys/s"
 # DRAM bytes per pair per onesweep launch from the committed ncu capture
 # (profiles/), or None before one exists.
-TRAFFIC_PER_PAIR_PASS = None
+TRAFFIC_PER_PAIR_PASS = 15.25  # DRAM bytes per pair per pass, 2^26 capture in profiles/dram_traffic_sort_scan_2p26.md
 
 
 def load_peaks():
