@@ -10,15 +10,19 @@
 //
 // B200 design:
 //  * One upfront histogram kernel reads every key once and counts the digits
-//    of all passes (grid = SMs x 4, warp-uniform fast path for skewed keys),
-//    then one tiny kernel turns the counts into per-pass digit starts.
+//    of all passes into lane-private shared-memory counter columns (no bank
+//    conflicts, skewed keys included), then one tiny kernel turns the counts
+//    into per-pass digit starts.
 //  * One onesweep kernel per 8-bit pass: 512 threads x 16 keys (8 for 64-bit
 //    keys) per tile, tile ids from an atomic ticket, warp-striped coalesced
-//    loads, stable in-warp ranking with __match_any_sync + per-warp shared
-//    counters, per-digit decoupled look-back over one 32-bit word per
-//    (tile, digit) {flags:2 | count:30} (64-bit words when n >= 2^30), then
-//    keys and values are placed in shared memory in digit order and written
-//    out with consecutive threads on consecutive addresses.
+//    loads, values of full tiles prefetched into shared memory by cp.async,
+//    per-warp digit counts published to the look-back before ranking, the
+//    per-digit windowed look-back (one 32-bit word per (tile, digit)
+//    {flags:2 | count:30}, 64-bit words when n >= 2^30) overlapped with the
+//    ranking of the other warps, stable ranking through per-warp atomicOr
+//    lane masks per digit, then keys and values placed in shared memory in
+//    digit order and written out with consecutive threads on consecutive
+//    addresses.
 //  * All look-back buffers of a sort are zeroed by one memset; no per-pass
 //    reset kernels (the reference resets 1 KiB per tile every pass).
 //  * Sizes are 64-bit in the ABI; no 2^28 "portions" (the reference's portion
@@ -35,8 +39,6 @@ constexpr int RS_DIGITS = 1 << RS_BITS;
 constexpr int RS_THREADS = 512;
 constexpr int RS_WARPS = RS_THREADS / 32;
 constexpr int RS_MAX_PASSES = 8;
-constexpr int HIST_THREADS = 512;
-constexpr int HIST_CTAS_PER_SM = 2;
 constexpr int RS_LB_WINDOW = 8;  // predecessor words loaded per look-back step
 
 template <typename KB> struct RsItems;
@@ -67,80 +69,75 @@ __device__ __forceinline__ uint32_t digit_of(KB k, uint32_t shift, uint32_t mask
     return (uint32_t)(ordered_bits<KB, KIND, DESC>(k) >> shift) & mask;
 }
 
-// ---------------------------------------------------------------------------
-// Histogram of all passes' digits.  bins[p*256 + d] += count.
-// ---------------------------------------------------------------------------
-template <typename KB, int KIND, bool DESC>
-__global__ void __launch_bounds__(HIST_THREADS)
-rs_histogram_kernel(const KB* __restrict__ keys, uint64_t n, uint32_t* __restrict__ bins,
-                    uint32_t begin_bit, uint32_t end_bit, uint32_t passes) {
-    __shared__ uint32_t sh[RS_MAX_PASSES][RS_DIGITS];
-    for (int i = threadIdx.x; i < RS_MAX_PASSES * RS_DIGITS; i += blockDim.x) (&sh[0][0])[i] = 0;
-    __syncthreads();
-    const int lane = threadIdx.x & 31;
+// Histogram of all passes' digits with lane-private counter columns: counter
+// (pass, digit) has COLS copies and lane L adds into copy L % COLS, so the
+// 32 atomics of a warp instruction fall into distinct banks whatever the
+// digits (skewed inputs included) — the shared-atomic bank conflicts that
+// bound a single-copy histogram disappear.  One 1024-thread CTA per SM,
+// 128 KiB of counters.  bins[p*256 + d] += count.
+constexpr int HISTC_THREADS = 1024;
+template <typename KB> struct HistCols { static constexpr int value = sizeof(KB) == 4 ? 32 : 16; };
+template <typename KB>
+constexpr size_t histc_smem_bytes() {
+    return (size_t)(sizeof(KB) * 8 / RS_BITS) * RS_DIGITS * HistCols<KB>::value * 4;
+}
 
-    // Count the digits of the N keys in k[] (all passes).  When every lane of
-    // the warp holds N valid keys with one and the same digit, lane 0 adds
-    // 32*N at once (skewed inputs would otherwise serialise on one counter).
-    auto count_keys = [&](const KB* k, int N, bool valid) {
-        KB o[16 / sizeof(KB)];
-        for (int v = 0; v < N; ++v) o[v] = ordered_bits<KB, KIND, DESC>(k[v]);
+template <typename KB, int KIND, bool DESC>
+__global__ void __launch_bounds__(HISTC_THREADS, 1)
+rs_histogram_cols_kernel(const KB* __restrict__ keys, uint64_t n, uint32_t* __restrict__ bins,
+                         uint32_t begin_bit, uint32_t end_bit, uint32_t passes) {
+    constexpr int COLS = HistCols<KB>::value;
+    extern __shared__ __align__(16) uint32_t hc[];  // [passes][256][COLS]
+    const uint32_t words = passes * RS_DIGITS * COLS;
+    for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) hc[i] = 0;
+    __syncthreads();
+    const uint32_t col = threadIdx.x & (COLS - 1);
+
+    auto count = [&](KB k) {
+        const KB o = ordered_bits<KB, KIND, DESC>(k);
 #pragma unroll
         for (uint32_t p = 0; p < RS_MAX_PASSES; ++p) {
             if (p >= passes) break;
             const uint32_t shift = begin_bit + p * RS_BITS;
             const uint32_t mask = (1u << min((uint32_t)RS_BITS, end_bit - shift)) - 1u;
-            uint32_t d[16 / sizeof(KB)];
-            bool same = valid;
-            for (int v = 0; v < N; ++v) {
-                d[v] = (uint32_t)(o[v] >> shift) & mask;
-                same = same && d[v] == d[0];
-            }
-            const uint32_t d00 = __shfl_sync(0xffffffffu, d[0], 0);
-            if (__all_sync(0xffffffffu, same && d[0] == d00)) {
-                if (lane == 0) atomicAdd(&sh[p][d00], 32u * N);
-            } else if (valid) {
-                for (int v = 0; v < N; ++v) atomicAdd(&sh[p][d[v]], 1u);
-            }
+            const uint32_t d = (uint32_t)(o >> shift) & mask;
+            atomicAdd(&hc[(p * RS_DIGITS + d) * COLS + col], 1u);
         }
     };
 
     constexpr int VEC = 16 / sizeof(KB);
-    constexpr int HU = 4;  // 16-byte loads in flight per thread
+    constexpr int HU = 4;
     const bool aligned = (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
     const uint64_t nvec = aligned ? n / VEC : 0;
     const uint4* vk = reinterpret_cast<const uint4*>(keys);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    // Whole warps iterate together so the warp-uniform fast path stays legal.
-    const uint64_t nvec_pad = (nvec + 31) / 32 * 32;
     uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    for (; i + (HU - 1) * stride < nvec_pad; i += HU * stride) {
+    for (; i + (HU - 1) * stride < nvec; i += HU * stride) {
         uint4 q[HU];
 #pragma unroll
-        for (int u = 0; u < HU; ++u) {
-            const uint64_t j = i + u * stride;
-            q[u] = j < nvec ? ld_stream(vk + j) : make_uint4(0, 0, 0, 0);
-        }
+        for (int u = 0; u < HU; ++u) q[u] = ld_stream(vk + i + u * stride);
 #pragma unroll
-        for (int u = 0; u < HU; ++u) count_keys(reinterpret_cast<const KB*>(&q[u]), VEC, i + u * stride < nvec);
+        for (int u = 0; u < HU; ++u) {
+            const KB* e = reinterpret_cast<const KB*>(&q[u]);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) count(e[v]);
+        }
     }
-    for (; i < nvec_pad; i += stride) {
-        const bool valid = i < nvec;
-        const uint4 q = valid ? ld_stream(vk + i) : make_uint4(0, 0, 0, 0);
-        count_keys(reinterpret_cast<const KB*>(&q), VEC, valid);
+    for (; i < nvec; i += stride) {
+        const uint4 q = ld_stream(vk + i);
+        const KB* e = reinterpret_cast<const KB*>(&q);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) count(e[v]);
     }
-    // Scalar tail (all keys when the base is not 16-byte aligned).
-    const uint64_t t0 = nvec * VEC;
-    const uint64_t ntail_pad = (n - t0 + 31) / 32 * 32;
-    for (i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ntail_pad; i += stride) {
-        const bool valid = t0 + i < n;
-        const KB k = valid ? keys[t0 + i] : KB(0);
-        count_keys(&k, 1, valid);
-    }
+    for (uint64_t t = nvec * VEC + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += stride)
+        count(keys[t]);
     __syncthreads();
-    for (uint32_t i = threadIdx.x; i < passes * RS_DIGITS; i += blockDim.x) {
-        const uint32_t c = (&sh[0][0])[i];
-        if (c) atomicAdd(bins + i, c);
+    // Fold the columns; thread j starts at column j % COLS so reads spread over the banks.
+    for (uint32_t b = threadIdx.x; b < passes * RS_DIGITS; b += blockDim.x) {
+        uint32_t sum = 0;
+#pragma unroll
+        for (int c = 0; c < COLS; ++c) sum += hc[b * COLS + ((c + b) & (COLS - 1))];
+        if (sum) atomicAdd(bins + b, sum);
     }
 }
 
@@ -473,14 +470,17 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
 
     const DeviceInfo di = device_info();
     {
-        const uint64_t per_cta = (uint64_t)HIST_THREADS * (16 / sizeof(KB)) * 4;
+        const uint64_t per_cta = (uint64_t)HISTC_THREADS * (16 / sizeof(KB)) * 4;
         uint64_t g = ceil_div(n, per_cta);
-        const uint64_t cap = (uint64_t)di.sms * HIST_CTAS_PER_SM;
+        const uint64_t cap = (uint64_t)di.sms;
         if (g > cap) g = cap;
         if (g == 0) g = 1;
+        constexpr size_t hsmem = histc_smem_bytes<KB>();
+        auto hk = rs_histogram_cols_kernel<KB, KIND, DESC>;
+        if (cudaFuncSetAttribute(hk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hsmem) != cudaSuccess)
+            return LCPP_ERR_CUDA;
         { ProfScope ps("rs_histogram", s);
-        rs_histogram_kernel<KB, KIND, DESC><<<(unsigned)g, HIST_THREADS, 0, s>>>(
-            (const KB*)keys_in, n, bins, begin_bit, end_bit, L.passes); }
+        hk<<<(unsigned)g, HISTC_THREADS, hsmem, s>>>((const KB*)keys_in, n, bins, begin_bit, end_bit, L.passes); }
         { ProfScope ps("rs_bins_scan", s);
         rs_bins_scan_kernel<<<L.passes, RS_DIGITS, 0, s>>>(bins); }
         count_launch(2);
