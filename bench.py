@@ -456,10 +456,18 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
     o = torch.empty(S, dtype=torch.float32, device=dev)
     tb = lib.lcpp_segment_reduce_temp_bytes(L.F32, N, S)
     t = torch.empty(tb, dtype=torch.uint8, device=dev)
+    lib.lcpp_profile_enable(1)
     ms = timeit(lambda: L.check(lib.lcpp_segment_reduce(0, L.F32, xs.data_ptr(), o.data_ptr(), S, b.data_ptr(),
                                                         e.data_ptr(), t.data_ptr(), tb, sh)), 20)
+    kern = {}
+    for kname in ("seg_warp", "seg_block"):
+        c, tt = L.C.c_uint64(0), L.C.c_double(0)
+        lib.lcpp_profile_read(kname.encode(), L.C.byref(c), L.C.byref(tt))
+        kern[kname + "_avg_ms"] = float(tt.value) / max(int(c.value), 1)
+    lib.lcpp_profile_enable(0)
     byts = 4 * N + 4 * (S + 1) + 4 * S  # values + CSR offsets + outputs
-    out["segment_sum_f32_2p27_2p20"] = {"ms": ms, "GB/s": byts / ms / 1e6, "frac": byts / ms / 1e6 / peak}
+    out[f"segment_sum_f32_2p{27 - shrink}_2p{20 - shrink}"] = {"ms": ms, "GB/s": byts / ms / 1e6,
+                                                              "frac": byts / ms / 1e6 / peak, **kern}
     return out
 
 
