@@ -145,3 +145,53 @@ def test_config3_keys_full_size_vs_oracle(cuda):
     got = abi_sort(keys)
     want = oracle.radix_sort(keys, threads=8)
     assert np.array_equal(got, want)
+
+
+def test_bucket_starts(cuda):
+    # run boundaries of keys partitioned by their top byte (multi-GPU sort helper)
+    import torch
+    from lc_parallel_primitive_b200 import _lib as L
+    from tests.helpers import stream
+
+    for kdt, bits in ((np.uint32, 32), (np.int32, 32), (np.uint64, 64)):
+        n = 300001
+        raw = G.u32(n, seed=21) if bits == 32 else G.u64(n, seed=21)
+        keys = raw.view(kdt)
+        part = abi_sort(keys, begin_bit=bits - 8, end_bit=bits)
+        d = torch.from_numpy(part.view(np.int32 if bits == 32 else np.int64)).to(cuda)
+        out = torch.empty(257, dtype=torch.int64, device=cuda)
+        dt = {np.uint32: L.U32, np.int32: L.I32, np.uint64: L.U64}[kdt]
+        L.check(L.lib().lcpp_radix_bucket_starts(dt, d.data_ptr(), n, bits - 8, out.data_ptr(), stream()))
+        got = out.cpu().numpy()
+        u = part.view(np.uint32 if bits == 32 else np.uint64).astype(np.uint64)
+        if kdt == np.int32:
+            u = u ^ np.uint64(1 << 31)
+        digit = (u >> np.uint64(bits - 8)) & np.uint64(0xFF)
+        want = np.searchsorted(digit, np.arange(257, dtype=np.uint64), side="left")
+        assert np.array_equal(got, want), kdt
+
+
+def test_keys_beyond_2p30_use_wide_lookback(cuda):
+    # n >= 2^30 switches the look-back words to 64 bits; check on the device:
+    # ascending order and an order-independent checksum of the multiset.
+    import torch
+    from lc_parallel_primitive_b200 import _lib as L
+    from tests.helpers import stream, temp
+
+    n = (1 << 30) + 12345
+    lib = L.lib()
+    keys = torch.randint(-(1 << 31), (1 << 31) - 1, (n,), dtype=torch.int32, device=cuda,
+                         generator=torch.Generator(device=cuda).manual_seed(3))
+    out = torch.empty_like(keys)
+    tb = lib.lcpp_radix_sort_temp_bytes(L.U32, L.NONE, n)
+    t = temp(tb)
+    L.check(lib.lcpp_radix_sort(L.U32, L.NONE, 0, keys.data_ptr(), out.data_ptr(), None, None, n, 0, 0,
+                                t.data_ptr(), tb, stream()))
+    torch.cuda.synchronize()
+    L.check(lib.lcpp_last_device_error(stream()))
+    del t
+    o = out.to(torch.int64) & 0xFFFFFFFF
+    assert bool((o[1:] >= o[:-1]).all())
+    ki = keys.to(torch.int64) & 0xFFFFFFFF
+    assert int(o.sum()) == int(ki.sum())
+    assert int((o * o % 1000003).sum()) == int((ki * ki % 1000003).sum())
