@@ -4,8 +4,8 @@
 // (src/lcpp/device/details/single_pass_scan_operator.h:138-251).
 //
 // B200 design:
-//  * 16384-item tiles (1024 threads x 16 items), 128-bit streaming loads and
-//    stores; each warp owns 512 contiguous items, each thread four 16-byte
+//  * 32768-item tiles (1024 threads x 32 items), 128-bit streaming loads and
+//    stores; each warp owns 1024 contiguous items, each thread eight 16-byte
 //    vectors at a 512-byte stride, so every load/store instruction is one
 //    fully coalesced 512-byte warp access.
 //  * Thread-local scans, then shuffle scans per vector, then a 32-entry scan of
@@ -25,9 +25,9 @@ namespace lcpp {
 constexpr int SCAN_THREADS = 1024;
 constexpr int SCAN_WARPS = SCAN_THREADS / 32;
 constexpr int SCAN_VECS = 8;                       // 16-byte vectors per thread
-constexpr int SCAN_ITEMS = SCAN_VECS * 4;          // 16 items (4-byte types)
-constexpr int SCAN_WARP_ITEMS = 32 * SCAN_ITEMS;   // 512
-constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 8192
+constexpr int SCAN_ITEMS = SCAN_VECS * 4;          // 32 items (4-byte types)
+constexpr int SCAN_WARP_ITEMS = 32 * SCAN_ITEMS;   // 1024
+constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 32768
 constexpr size_t SCAN_HDR = 256;                   // ticket counter + padding
 constexpr int SCAN_DESC_TILE = 8192;               // smallest tile of any scan kernel: sizes the descriptors
 
