@@ -441,7 +441,10 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     out = {}
+    # L2 flush between timed iterations: write a 256 MiB buffer (> 126 MB L2), then read
+    # another one so the dirty lines are written back before the timed region starts.
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_rd = torch.ones(64 << 20, dtype=torch.float32, device=dev)
 
     def timeit(fn, iters, flush_l2=False):
         for _ in range(3):
@@ -451,6 +454,7 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
         for _ in range(iters):
             if flush_l2:
                 flush.zero_()
+                flush_rd.sum()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             fn()
@@ -479,9 +483,14 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
         o = torch.empty(1, dtype=torch.int32, device=dev)
         tb = lib.lcpp_reduce_temp_bytes(L.I32, n)
         t = torch.empty(tb, dtype=torch.uint8, device=dev)
+        lib.lcpp_profile_enable(1)
         ms = timeit(lambda: L.check(lib.lcpp_reduce(0, L.I32, xr.data_ptr(), o.data_ptr(), n, t.data_ptr(), tb, sh)),
                     30, flush_l2=True)
-        out[f"reduce_sum_i32_2p{logn}"] = {"ms": ms, "GB/s": 4 * n / ms / 1e6, "frac": 4 * n / ms / 1e6 / peak}
+        c, tt = L.C.c_uint64(0), L.C.c_double(0)
+        lib.lcpp_profile_read(b"reduce", L.C.byref(c), L.C.byref(tt))
+        lib.lcpp_profile_enable(0)
+        out[f"reduce_sum_i32_2p{logn}"] = {"ms": ms, "GB/s": 4 * n / ms / 1e6, "frac": 4 * n / ms / 1e6 / peak,
+                                           "kernels_avg_ms": float(tt.value) / max(int(c.value), 1)}
     del x
 
     # segment reduce: 2^27 f32, 2^20 lognormal segments

@@ -73,6 +73,11 @@ reduce_kernel(const T* __restrict__ in, uint64_t n, T* __restrict__ partials,
     if (tail0 + gtid < n) acc = Op::template apply<T>(acc, in[tail0 + gtid]);
 
     acc = block_reduce<Op>(acc, s_warp);
+    if (!ticket) {  // two-kernel form: reduce_final_kernel combines the partials
+        if (threadIdx.x == 0) partials[blockIdx.x] = acc;
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        return;
+    }
     if (threadIdx.x == 0) {
         partials[blockIdx.x] = acc;
         __threadfence();
@@ -88,6 +93,48 @@ reduce_kernel(const T* __restrict__ in, uint64_t n, T* __restrict__ partials,
     __syncthreads();  // s_warp reuse
     v = block_reduce<Op>(v, s_warp);
     if (threadIdx.x == 0) out[0] = Op::template apply<T>(init, v);
+}
+
+// Second kernel of the two-kernel form, launched with programmatic dependent
+// launch so that its launch overlaps the partial-sum kernel:
+// griddepcontrol.wait blocks until that kernel has completed and its writes
+// are visible.  One CTA combines the partials in a fixed order.
+template <typename Op, typename T>
+__global__ void __launch_bounds__(REDUCE_THREADS)
+reduce_final_kernel(const T* __restrict__ partials, unsigned int count, T* __restrict__ out, T init) {
+    __shared__ T s_warp[REDUCE_THREADS / 32];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    T v = Op::template identity<T>();
+    for (unsigned int b = threadIdx.x; b < count; b += blockDim.x) v = Op::template apply<T>(v, partials[b]);
+    v = block_reduce<Op>(v, s_warp);
+    if (threadIdx.x == 0) out[0] = Op::template apply<T>(init, v);
+}
+
+template <typename Op, typename T>
+static lcpp_status reduce_two_kernels(const T* in, uint64_t n, T* part, T* out, unsigned grid, cudaStream_t s) {
+    reduce_kernel<Op, T><<<grid, REDUCE_THREADS, 0, s>>>(in, n, part, nullptr, out, Op::template identity<T>());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(REDUCE_THREADS);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, reduce_final_kernel<Op, T>, (const T*)part, grid, out, Op::template identity<T>()) !=
+        cudaSuccess)
+        return LCPP_ERR_CUDA;
+    count_launch(2);
+    return check_launch();
+}
+
+static bool reduce_use_pdl() {
+    static const bool on = [] {
+        const char* e = getenv("LCPP_REDUCE_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 static unsigned int reduce_grid(uint64_t n, int elem_size) {
@@ -121,7 +168,8 @@ extern "C" lcpp_status lcpp_reduce(int op, int dtype, const void* in, void* out,
     cudaStream_t s = (cudaStream_t)stream;
     unsigned int* ticket = (unsigned int*)temp;
     void* partials = (char*)temp + 256;
-    if (cudaMemsetAsync(ticket, 0, sizeof(unsigned int), s) != cudaSuccess) return LCPP_ERR_CUDA;
+    const bool pdl = reduce_use_pdl();
+    if (!pdl && cudaMemsetAsync(ticket, 0, sizeof(unsigned int), s) != cudaSuccess) return LCPP_ERR_CUDA;
     return dispatch_dtype(dtype, [&](auto zero) -> lcpp_status {
         using T = decltype(zero);
         const unsigned int grid = reduce_grid(n, sizeof(T));
@@ -129,6 +177,13 @@ extern "C" lcpp_status lcpp_reduce(int op, int dtype, const void* in, void* out,
         T* pout = (T*)out;
         T* part = (T*)partials;
         ProfScope ps("reduce", s);
+        if (pdl) {
+            switch (op) {
+                case LCPP_OP_SUM: return reduce_two_kernels<OpSum, T>(pin, n, part, pout, grid, s);
+                case LCPP_OP_MIN: return reduce_two_kernels<OpMin, T>(pin, n, part, pout, grid, s);
+                default: return reduce_two_kernels<OpMax, T>(pin, n, part, pout, grid, s);
+            }
+        }
         switch (op) {
             case LCPP_OP_SUM:
                 reduce_kernel<OpSum, T><<<grid, REDUCE_THREADS, 0, s>>>(pin, n, part, ticket, pout, OpSum::identity<T>());
