@@ -45,7 +45,33 @@ class DeviceReduce : public LuisaModule {
         record(cmdlist, LCPP_OP_MAX, temp_storage, d_in, d_out, num_item);
     }
 
+    // Reference: device_reduce.h:93-108, 187-275.  Ties: ArgMin the first
+    // minimum, ArgMax the last maximum (ArgMinOp / ArgMaxOp).
+    template <typename Type4Byte>
+    static size_t GetArgTempStorageBytes(size_t num_item) {
+        return lcpp_arg_reduce_temp_bytes(lcpp_dtype_of<Type4Byte>(), num_item);
+    }
+    template <NumericT Type4Byte>
+    void ArgMin(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+                BufferView<Type4Byte> d_out, BufferView<uint> d_index_out, size_t num_item) {
+        record_arg(cmdlist, LCPP_OP_MIN, temp_storage, d_in, d_out, d_index_out, num_item);
+    }
+    template <NumericT Type4Byte>
+    void ArgMax(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+                BufferView<Type4Byte> d_out, BufferView<uint> d_index_out, size_t num_item) {
+        record_arg(cmdlist, LCPP_OP_MAX, temp_storage, d_in, d_out, d_index_out, num_item);
+    }
+
   private:
+    template <typename T>
+    void record_arg(CommandList& cmdlist, int op, BufferView<uint> temp, BufferView<T> in, BufferView<T> out,
+                    BufferView<uint> idx, size_t n) {
+        cmdlist << [=](cudaStream_t s) {
+            return lcpp_arg_reduce(op, lcpp_dtype_of<T>(), in.data(), out.data(), idx.data(), n, temp.data(),
+                                   temp.size_bytes(), s);
+        };
+        lcpp_check(cmdlist, m_debug_stream);
+    }
     template <typename T>
     void record(CommandList& cmdlist, int op, BufferView<uint> temp, BufferView<T> in, BufferView<T> out,
                 size_t n) {

@@ -57,6 +57,39 @@ class DeviceSegmentReduce : public LuisaModule {
     LCPP_SEGMENT_OP(Max, LCPP_OP_MAX)  // empty segment -> lowest() (device_segment_reduce.h:186-194)
 #undef LCPP_SEGMENT_OP
 
+    // ArgMin / ArgMax per segment, index relative to the segment begin
+    // (device_segment_reduce.h:197-349).  No temp needed; the size function
+    // is kept for the reference's call sequence.
+    template <typename Type4Byte>
+    static size_t GetArgTempStorageBytes(size_t /*num_item*/, size_t /*num_segments*/) { return 0; }
+
+#define LCPP_SEGMENT_ARG(NAME, OP)                                                                             \
+    template <NumericT ValueType>                                                                              \
+    void NAME(CommandList& cmdlist, BufferView<uint> /*temp_storage*/, BufferView<ValueType> d_in,             \
+              BufferView<ValueType> d_out, BufferView<uint> d_index_out, uint num_segments,                    \
+              BufferView<uint> d_begin_offsets, BufferView<uint> d_end_offsets) {                              \
+        cmdlist << [=](cudaStream_t s) {                                                                       \
+            return lcpp_segment_arg_reduce(OP, lcpp_dtype_of<ValueType>(), d_in.data(), d_out.data(),          \
+                                           d_index_out.data(), num_segments, d_begin_offsets.data(),           \
+                                           d_end_offsets.data(), s);                                           \
+        };                                                                                                     \
+        lcpp_check(cmdlist, m_debug_stream);                                                                   \
+    }                                                                                                          \
+    template <NumericT ValueType>                                                                              \
+    void NAME(CommandList& cmdlist, BufferView<uint> /*temp_storage*/, BufferView<ValueType> d_in,             \
+              BufferView<ValueType> d_out, BufferView<uint> d_index_out, uint num_segments,                    \
+              uint segment_size) {                                                                             \
+        cmdlist << [=](cudaStream_t s) {                                                                       \
+            return lcpp_segment_arg_reduce_fixed(OP, lcpp_dtype_of<ValueType>(), d_in.data(), d_out.data(),    \
+                                                 d_index_out.data(), num_segments, segment_size, s);           \
+        };                                                                                                     \
+        lcpp_check(cmdlist, m_debug_stream);                                                                   \
+    }
+
+    LCPP_SEGMENT_ARG(ArgMin, LCPP_OP_MIN)
+    LCPP_SEGMENT_ARG(ArgMax, LCPP_OP_MAX)
+#undef LCPP_SEGMENT_ARG
+
   private:
     Device m_device;
     Stream* m_debug_stream = nullptr;

@@ -160,6 +160,26 @@ uint64_t    lcpp_scan_noalloc_max_items(void);
 lcpp_status lcpp_scan_noalloc(int kind, int dtype, const void* in, void* out, uint64_t n,
                               void* stream);
 
+/* ---- ArgMin / ArgMax ---------------------------------------------------
+ * Value and index of the minimum / maximum.  Replaces DeviceReduce::ArgMin/
+ * ArgMax and GetArgTempStorageBytes (device_reduce.h:93-108,187-275) and
+ * DeviceSegmentReduce::ArgMin/ArgMax (device_segment_reduce.h:197-349).
+ * Ties follow the reference's ArgMinOp / ArgMaxOp (thread_operators.h:19-47):
+ * ArgMin returns the smallest index, ArgMax the largest.  Segment indices are
+ * relative to the segment begin.  Empty input / segment: index 1 and
+ * value max() (ArgMin) or lowest() (ArgMax).  op: LCPP_OP_MIN or LCPP_OP_MAX;
+ * dtype: any of I32 U32 F32 I64 U64 F64; n < 2^32. */
+size_t      lcpp_arg_reduce_temp_bytes(int dtype, uint64_t n);
+lcpp_status lcpp_arg_reduce(int op, int dtype, const void* in, void* out_value, uint32_t* out_index,
+                            uint64_t n, void* temp, size_t temp_bytes, void* stream);
+lcpp_status lcpp_segment_arg_reduce(int op, int dtype, const void* in, void* out_value,
+                                    uint32_t* out_index, uint64_t num_segments,
+                                    const uint32_t* begin_offsets, const uint32_t* end_offsets,
+                                    void* stream);
+lcpp_status lcpp_segment_arg_reduce_fixed(int op, int dtype, const void* in, void* out_value,
+                                          uint32_t* out_index, uint64_t num_segments,
+                                          uint64_t segment_size, void* stream);
+
 /* ---- Device error word --------------------------------------------------
  * Synchronizes `stream`, returns the first device-side error latched since
  * the last call on the current device (LCPP_OK if none) and clears it.  The

@@ -46,6 +46,10 @@ SIGNATURES = {
     "lcpp_segment_reduce_temp_bytes": (_sz, [_i, _u64, _u64]),
     "lcpp_segment_reduce": (_i, [_i, _i, _vp, _vp, _u64, _vp, _vp, _vp, _sz, _vp]),
     "lcpp_segment_reduce_fixed": (_i, [_i, _i, _vp, _vp, _u64, _u64, _vp]),
+    "lcpp_arg_reduce_temp_bytes": (_sz, [_i, _u64]),
+    "lcpp_arg_reduce": (_i, [_i, _i, _vp, _vp, _vp, _u64, _vp, _sz, _vp]),
+    "lcpp_segment_arg_reduce": (_i, [_i, _i, _vp, _vp, _vp, _u64, _vp, _vp, _vp]),
+    "lcpp_segment_arg_reduce_fixed": (_i, [_i, _i, _vp, _vp, _vp, _u64, _u64, _vp]),
     "lcpp_last_device_error": (_i, [_vp]),
     "lcpp_lookback_temp_bytes": (_sz, [_u64]),
     "lcpp_lookback_tiles": (_i, [_vp, _vp, _vp, _u64, _vp, _sz, _vp]),

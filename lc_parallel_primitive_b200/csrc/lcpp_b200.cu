@@ -6,4 +6,5 @@
 #include "scan_pipe.cu"
 #include "radix_sort.cu"
 #include "segment_reduce.cu"
+#include "arg_reduce.cu"
 #include "scan_noalloc.cu"

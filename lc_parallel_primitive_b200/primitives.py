@@ -171,6 +171,23 @@ class DeviceReduce(_Module):
     def Max(self, cmdlist, temp_storage, d_in, d_out, num_item):
         self.Reduce(cmdlist, temp_storage, d_in, d_out, num_item, L.OP_MAX)
 
+    @staticmethod
+    def GetArgTempStorageBytes(num_item: int, dtype=torch.int32) -> int:
+        return int(L.lib().lcpp_arg_reduce_temp_bytes(lcpp_dtype(dtype), num_item))
+
+    def _arg(self, cmdlist, temp_storage, d_in, d_out, d_index_out, num_item, op):
+        dt = lcpp_dtype(d_in)
+        pin, pout, pidx = _ptr(d_in), _ptr(d_out), _ptr(d_index_out)
+        ptmp, nt = _ptr(temp_storage), _nbytes(temp_storage)
+        self._record(cmdlist, lambda s: L.lib().lcpp_arg_reduce(op, dt, pin, pout, pidx, num_item, ptmp, nt, s),
+                     "DeviceReduce.Arg")
+
+    def ArgMin(self, cmdlist, temp_storage, d_in, d_out, d_index_out, num_item):
+        self._arg(cmdlist, temp_storage, d_in, d_out, d_index_out, num_item, L.OP_MIN)
+
+    def ArgMax(self, cmdlist, temp_storage, d_in, d_out, d_index_out, num_item):
+        self._arg(cmdlist, temp_storage, d_in, d_out, d_index_out, num_item, L.OP_MAX)
+
 
 class DeviceScan(_Module):
     @staticmethod
@@ -259,6 +276,27 @@ class DeviceSegmentReduce(_Module):
     def Max(self, cmdlist, temp_storage, d_in, d_out, num_segments, d_begin_offsets_or_size, d_end_offsets=None):
         self.Reduce(cmdlist, temp_storage, d_in, d_out, num_segments, d_begin_offsets_or_size, d_end_offsets,
                     L.OP_MAX)
+
+
+def _segment_arg(self, cmdlist, d_in, d_out, d_index_out, num_segments, begin_or_size, d_end_offsets, op):
+    dt = lcpp_dtype(d_in)
+    pin, pout, pidx = _ptr(d_in), _ptr(d_out), _ptr(d_index_out)
+    if d_end_offsets is None:
+        size = int(begin_or_size)
+        self._record(cmdlist, lambda s: L.lib().lcpp_segment_arg_reduce_fixed(op, dt, pin, pout, pidx,
+                                                                              num_segments, size, s),
+                     "DeviceSegmentReduce.Arg")
+        return
+    pb, pe = _ptr(begin_or_size), _ptr(d_end_offsets)
+    self._record(cmdlist, lambda s: L.lib().lcpp_segment_arg_reduce(op, dt, pin, pout, pidx, num_segments, pb, pe, s),
+                 "DeviceSegmentReduce.Arg")
+
+
+DeviceSegmentReduce.GetArgTempStorageBytes = staticmethod(lambda num_item, num_segments=0, dtype=None: 0)
+DeviceSegmentReduce.ArgMin = lambda self, cmdlist, temp_storage, d_in, d_out, d_index_out, num_segments, b, e=None: \
+    _segment_arg(self, cmdlist, d_in, d_out, d_index_out, num_segments, b, e, L.OP_MIN)
+DeviceSegmentReduce.ArgMax = lambda self, cmdlist, temp_storage, d_in, d_out, d_index_out, num_segments, b, e=None: \
+    _segment_arg(self, cmdlist, d_in, d_out, d_index_out, num_segments, b, e, L.OP_MAX)
 
 
 def temp_buffer(nbytes: int, device="cuda") -> torch.Tensor:

@@ -38,11 +38,13 @@ def lib():
         h.oracle_radix_sort.argtypes = [i, i, i, vp, vp, vp, vp, u64, i, i, i]
         h.oracle_segment_reduce.argtypes = [i, i, vp, vp, u64, vp, vp]
         h.oracle_reduce_sum_mt.argtypes = [i, vp, u64, vp, i]
+        h.oracle_arg_reduce.argtypes = [i, i, vp, u64, vp, vp]
+        h.oracle_segment_arg_reduce.argtypes = [i, i, vp, vp, vp, u64, vp, vp]
         h.oracle_scan_mt.argtypes = [i, i, vp, vp, u64, i]
         h.oracle_segment_reduce_mt.argtypes = [i, i, vp, vp, u64, vp, vp, i]
         for f in ("oracle_reduce", "oracle_scan", "oracle_abs_prefix_f32", "oracle_radix_sort",
                   "oracle_segment_reduce", "oracle_reduce_sum_mt", "oracle_scan_mt",
-                  "oracle_segment_reduce_mt"):
+                  "oracle_segment_reduce_mt", "oracle_arg_reduce", "oracle_segment_arg_reduce"):
             getattr(h, f).restype = i
         _lib = h
     return _lib
@@ -125,3 +127,23 @@ def segment_reduce_mt(op: int, x, begin, end, out, threads: int):
     _ok(lib().oracle_segment_reduce_mt(op, _dt(x), _p(x), _p(out), begin.size, _p(begin), _p(end), threads),
         "segment_reduce_mt")
     return out
+
+
+def arg_reduce(op: int, x: np.ndarray):
+    """(value, index) of the min (op=OP_MIN, first index) or max (OP_MAX, last index)."""
+    x = np.ascontiguousarray(x)
+    v = np.zeros(1, dtype=x.dtype)
+    i = np.zeros(1, dtype=np.uint32)
+    _ok(lib().oracle_arg_reduce(op, _dt(x), _p(x), x.size, _p(v), _p(i)), "arg_reduce")
+    return v[0], int(i[0])
+
+
+def segment_arg_reduce(op: int, x: np.ndarray, begin: np.ndarray, end: np.ndarray):
+    x = np.ascontiguousarray(x)
+    begin = np.ascontiguousarray(begin, dtype=np.uint32)
+    end = np.ascontiguousarray(end, dtype=np.uint32)
+    v = np.empty(begin.size, dtype=x.dtype)
+    i = np.empty(begin.size, dtype=np.uint32)
+    _ok(lib().oracle_segment_arg_reduce(op, _dt(x), _p(x), _p(v), _p(i), begin.size, _p(begin), _p(end)),
+        "segment_arg_reduce")
+    return v, i

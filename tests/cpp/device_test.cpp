@@ -219,6 +219,54 @@ int main(int argc, char* argv[]) {
         }
     }
 
+    // ---- device_reduce_test.cpp:168-220 / device_segment_reduce.cpp:179-293: Arg* --
+    {
+        const int N = 1 << 12;
+        std::vector<int32> input(N);
+        std::iota(input.begin(), input.end(), 0);
+        std::mt19937 rng(114521);
+        std::shuffle(input.begin(), input.end(), rng);
+        DeviceReduce<> reducer;
+        reducer.create(device, &stream);
+        auto in = device.create_buffer<int32>(N);
+        auto out = device.create_buffer<int32>(1);
+        auto idx = device.create_buffer<uint>(1);
+        stream << in.copy_from(input.data()) << synchronize();
+        auto temp = device.create_buffer<uint>(bytes_to_uint_count(DeviceReduce<>::GetArgTempStorageBytes<int32>(N)));
+        CommandList cmdlist;
+        std::vector<uint> ri(1);
+        reducer.ArgMin(cmdlist, temp.view(), in.view(), out.view(), idx.view(), in.size());
+        stream << cmdlist.commit() << synchronize() << idx.copy_to(ri.data()) << synchronize();
+        EXPECT(ri[0] == (uint)(std::min_element(input.begin(), input.end()) - input.begin()), "argmin %u", ri[0]);
+        reducer.ArgMax(cmdlist, temp.view(), in.view(), out.view(), idx.view(), in.size());
+        stream << cmdlist.commit() << synchronize() << idx.copy_to(ri.data()) << synchronize();
+        EXPECT(ri[0] == (uint)(std::max_element(input.begin(), input.end()) - input.begin()), "argmax %u", ri[0]);
+
+        const int per = 100, S = N / per + 1;
+        std::vector<uint> b(S), e(S);
+        for (int s = 0; s < S; s++) { b[s] = s * per; e[s] = std::min(s * per + per, N); }
+        DeviceSegmentReduce<> sr;
+        sr.create(device, &stream);
+        auto sv = device.create_buffer<int32>(S);
+        auto si = device.create_buffer<uint>(S);
+        auto bb = device.create_buffer<uint>(S), eb = device.create_buffer<uint>(S);
+        stream << bb.copy_from(b.data()) << eb.copy_from(e.data()) << synchronize();
+        std::vector<int32> rv(S);
+        std::vector<uint> rix(S);
+        sr.ArgMax(cmdlist, temp.view(), in.view(), sv.view(), si.view(), S, bb.view(), eb.view());
+        stream << cmdlist.commit() << synchronize() << sv.copy_to(rv.data()) << si.copy_to(rix.data()) << synchronize();
+        for (int s = 0; s < S; s++) {
+            auto m = std::max_element(input.begin() + b[s], input.begin() + e[s]);
+            EXPECT(rv[s] == *m && rix[s] == (uint)(m - input.begin() - b[s]), "segment argmax %d", s);
+        }
+        sr.ArgMin(cmdlist, temp.view(), in.view(), sv.view(), si.view(), S, bb.view(), eb.view());
+        stream << cmdlist.commit() << synchronize() << sv.copy_to(rv.data()) << si.copy_to(rix.data()) << synchronize();
+        for (int s = 0; s < S; s++) {
+            auto m = std::min_element(input.begin() + b[s], input.begin() + e[s]);
+            EXPECT(rv[s] == *m && rix[s] == (uint)(m - input.begin() - b[s]), "segment argmin %d", s);
+        }
+    }
+
     EXPECT(stream.last_status() == 0, "stream status %d", stream.last_status());
     std::printf("%s: %d failure(s)\n", g_failures ? "FAILED" : "OK", g_failures);
     return g_failures ? 1 : 0;
