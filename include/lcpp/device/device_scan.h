@@ -34,7 +34,30 @@ class DeviceScan : public LuisaModule {
         record(cmdlist, LCPP_SCAN_INCLUSIVE, temp_storage, d_in, d_out, num_items);
     }
 
+    // Reference: device_scan.h:114-178.  ScanOp must be SumOp, MinOp or MaxOp
+    // (DSL lambdas cannot be passed to precompiled kernels).
+    template <NumericT Type4Byte, typename ScanOp>
+    void ExclusiveScan(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+                       BufferView<Type4Byte> d_out, size_t num_items, ScanOp, Type4Byte initial_value) {
+        record_op(cmdlist, LCPP_SCAN_EXCLUSIVE, ScanOp::lcpp_op, temp_storage, d_in, d_out, num_items, initial_value);
+    }
+    template <NumericT Type4Byte, typename ScanOp>
+    void InclusiveScan(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+                       BufferView<Type4Byte> d_out, size_t num_items, ScanOp, Type4Byte initial_value) {
+        record_op(cmdlist, LCPP_SCAN_INCLUSIVE, ScanOp::lcpp_op, temp_storage, d_in, d_out, num_items, initial_value);
+    }
+
   private:
+    template <typename T>
+    void record_op(CommandList& cmdlist, int kind, int op, BufferView<uint> temp, BufferView<T> in,
+                   BufferView<T> out, size_t n, T init) {
+        static_assert(sizeof(T) == 4, "DeviceScan serves 4-byte types");
+        cmdlist << [=](cudaStream_t s) {
+            return lcpp_scan_op(kind, op, lcpp_dtype_of<T>(), in.data(), out.data(), n, &init, temp.data(),
+                                temp.size_bytes(), s);
+        };
+        lcpp_check(cmdlist, m_debug_stream);
+    }
     template <typename T>
     void record(CommandList& cmdlist, int kind, BufferView<uint> temp, BufferView<T> in, BufferView<T> out,
                 size_t n) {

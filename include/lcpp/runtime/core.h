@@ -224,6 +224,12 @@ constexpr int lcpp_dtype_of() {
     else return -1;
 }
 
+// Reduction / scan operators of the reference (common/thread_operators.h:
+// SumOp, MinOp, MaxOp).  Here they only select the kernel's operator.
+struct SumOp { static constexpr int lcpp_op = LCPP_OP_SUM; };
+struct MinOp { static constexpr int lcpp_op = LCPP_OP_MIN; };
+struct MaxOp { static constexpr int lcpp_op = LCPP_OP_MAX; };
+
 template <typename T>
 concept NumericT = std::is_integral_v<T> || std::is_floating_point_v<T>;
 

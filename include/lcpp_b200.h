@@ -93,6 +93,15 @@ lcpp_status lcpp_scan_carry(int kind, int dtype, const void* in, void* out, uint
                             const void* carry_in, void* temp, size_t temp_bytes,
                             void* stream);
 
+/* Exclusive / inclusive scan with op in {LCPP_OP_SUM, LCPP_OP_MIN, LCPP_OP_MAX}
+ * and an initial value: out[i] = init (+) in[0] (+) ... (+) in[i-1]
+ * (exclusive; out[0] = init) or ... (+) in[i] (inclusive).  init is a HOST
+ * pointer to one element of dtype (NULL = the op's identity).  Replaces
+ * DeviceScan::ExclusiveScan / InclusiveScan with SumOp / MinOp / MaxOp
+ * (device_scan.h:114-178); arbitrary DSL lambdas cannot cross a C ABI. */
+lcpp_status lcpp_scan_op(int kind, int op, int dtype, const void* in, void* out, uint64_t n,
+                         const void* init, void* temp, size_t temp_bytes, void* stream);
+
 /* ---- DeviceRadixSort ----------------------------------------------------
  * Stable LSD radix sort (8-bit digits, onesweep) of keys[begin_bit,end_bit),
  * values travelling with their keys.  keys_in/values_in are not modified.

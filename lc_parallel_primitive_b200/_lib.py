@@ -38,6 +38,7 @@ SIGNATURES = {
     "lcpp_scan_temp_bytes": (_sz, [_i, _u64]),
     "lcpp_scan": (_i, [_i, _i, _vp, _vp, _u64, _vp, _sz, _vp]),
     "lcpp_scan_carry": (_i, [_i, _i, _vp, _vp, _u64, _vp, _vp, _sz, _vp]),
+    "lcpp_scan_op": (_i, [_i, _i, _i, _vp, _vp, _u64, _vp, _vp, _sz, _vp]),
     "lcpp_scan_noalloc_max_items": (_u64, []),
     "lcpp_scan_noalloc": (_i, [_i, _i, _vp, _vp, _u64, _vp]),
     "lcpp_radix_sort_temp_bytes": (_sz, [_i, _i, _u64]),

@@ -31,8 +31,8 @@ constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 32768
 constexpr size_t SCAN_HDR = 256;                   // ticket counter + padding
 constexpr int SCAN_DESC_TILE = 8192;               // smallest tile of any scan kernel: sizes the descriptors
 
-template <typename T>
-static lcpp_status scan_pipe_launch(bool inclusive, const T* in, T* out, uint64_t n, const T* carry_in,
+template <typename Op, typename T>
+static lcpp_status scan_pipe_launch(bool inclusive, const T* in, T* out, uint64_t n, const T* carry_in, T init,
                                     unsigned int* ticket, uint64_t* desc, cudaStream_t s);
 
 constexpr uint64_t ST_PARTIAL = 1ull << 32;
@@ -45,7 +45,6 @@ template <typename T> __device__ __forceinline__ T from_bits(uint32_t b) { retur
 template <> __device__ __forceinline__ uint32_t from_bits<uint32_t>(uint32_t b) { return b; }
 template <> __device__ __forceinline__ int32_t from_bits<int32_t>(uint32_t b) { return (int32_t)b; }
 
-template <typename T> __device__ __forceinline__ T add(T a, T b) { return OpSum::apply<T>(a, b); }
 
 __device__ __forceinline__ void backoff(uint32_t it) {
     if (it > 64) __nanosleep(it < 1024 ? 32 : 128);
@@ -55,19 +54,19 @@ __device__ __forceinline__ void backoff(uint32_t it) {
 // aggregates of all preceding tiles (same value in every lane).  Lane L
 // inspects tile (window_end - L); windows of 32 move towards tile 0 until an
 // inclusive descriptor is found.
-template <typename T>
+template <typename Op, typename T>
 __device__ T lookback_warp(const uint64_t* desc, int64_t tile) {
     const int lane = threadIdx.x & 31;
     const uint32_t limit = g_spin_limit;
-    T acc = T(0);
+    T acc = Op::template identity<T>();
     int64_t p = tile - 1 - lane;
     uint32_t spins = 0;
     while (true) {
-        uint64_t d = p >= 0 ? ld_relaxed_u64(desc + p) : ST_INCLUSIVE;
+        uint64_t d = p >= 0 ? ld_relaxed_u64(desc + p) : (ST_INCLUSIVE | to_bits<T>(Op::template identity<T>()));
         while (__any_sync(0xffffffffu, (d >> 32) == 0)) {
             if (++spins > limit) {
                 if (lane == 0) set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
-                return warp_reduce<OpSum>(acc);
+                return warp_reduce<Op>(acc);
             }
             backoff(spins);
             if ((d >> 32) == 0) d = ld_relaxed_u64(desc + p);
@@ -76,32 +75,32 @@ __device__ T lookback_warp(const uint64_t* desc, int64_t tile) {
         T v = from_bits<T>((uint32_t)d);
         if (incl) {
             const int first = __ffs(incl) - 1;
-            if (lane > first) v = T(0);
-            return add(acc, warp_reduce<OpSum>(v));
+            if (lane > first) v = Op::template identity<T>();
+            return Op::template apply<T>(acc, warp_reduce<Op>(v));
         }
-        acc = add(acc, warp_reduce<OpSum>(v));
+        acc = Op::template apply<T>(acc, warp_reduce<Op>(v));
         p -= 32;
     }
 }
 
 // Warp 0 of a tile: publish the tile aggregate, resolve the exclusive prefix,
 // publish the inclusive value.  Returns the exclusive prefix in every lane.
-template <typename T>
+template <typename Op, typename T>
 __device__ __forceinline__ T tile_prefix(uint64_t* desc, int64_t tile, T aggregate, T carry) {
     const int lane = threadIdx.x & 31;
     if (tile == 0) {
-        if (lane == 0) st_relaxed_u64(desc, ST_INCLUSIVE | to_bits<T>(add(carry, aggregate)));
+        if (lane == 0) st_relaxed_u64(desc, ST_INCLUSIVE | to_bits<T>(Op::template apply<T>(carry, aggregate)));
         return carry;
     }
     if (lane == 0) st_relaxed_u64(desc + tile, ST_PARTIAL | to_bits<T>(aggregate));
-    const T excl = lookback_warp<T>(desc, tile);
-    if (lane == 0) st_relaxed_u64(desc + tile, ST_INCLUSIVE | to_bits<T>(add(excl, aggregate)));
+    const T excl = lookback_warp<Op, T>(desc, tile);
+    if (lane == 0) st_relaxed_u64(desc + tile, ST_INCLUSIVE | to_bits<T>(Op::template apply<T>(excl, aggregate)));
     return excl;
 }
 
-template <typename T, bool INCLUSIVE>
+template <typename Op, typename T, bool INCLUSIVE>
 __global__ void __launch_bounds__(SCAN_THREADS, 1)
-scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in,
+scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in, T init,
             unsigned int* ticket, uint64_t* desc) {
     __shared__ unsigned int s_tile;
     __shared__ T s_warp[SCAN_WARPS];
@@ -130,47 +129,47 @@ scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in,
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const uint64_t i = base + j * 128 + k;
-                x[j][k] = i < n ? in[i] : T(0);
+                x[j][k] = i < n ? in[i] : Op::template identity<T>();
             }
     }
 
     // Thread-local inclusive scans, then one warp scan per vector.
     T pre[SCAN_VECS];  // exclusive prefix of each vector within the warp
-    T carry = T(0);
+    T carry = Op::template identity<T>();
 #pragma unroll
     for (int j = 0; j < SCAN_VECS; ++j) {
 #pragma unroll
-        for (int k = 1; k < 4; ++k) x[j][k] = add(x[j][k - 1], x[j][k]);
+        for (int k = 1; k < 4; ++k) x[j][k] = Op::template apply<T>(x[j][k - 1], x[j][k]);
         T incl = x[j][3];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const T y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl = add(y, incl);
+            if (lane >= o) incl = Op::template apply<T>(y, incl);
         }
         T excl = __shfl_up_sync(0xffffffffu, incl, 1);
-        if (lane == 0) excl = T(0);
-        pre[j] = add(carry, excl);
-        carry = add(carry, __shfl_sync(0xffffffffu, incl, 31));
+        if (lane == 0) excl = Op::template identity<T>();
+        pre[j] = Op::template apply<T>(carry, excl);
+        carry = Op::template apply<T>(carry, __shfl_sync(0xffffffffu, incl, 31));
     }
     if (lane == 0) s_warp[warp] = carry;
     __syncthreads();
 
     if (warp == 0) {
-        const T wt = lane < SCAN_WARPS ? s_warp[lane] : T(0);
+        const T wt = lane < SCAN_WARPS ? s_warp[lane] : Op::template identity<T>();
         T incl = wt;
 #pragma unroll
         for (int o = 1; o < SCAN_WARPS; o <<= 1) {
             const T y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl = add(y, incl);
+            if (lane >= o) incl = Op::template apply<T>(y, incl);
         }
         const T aggregate = __shfl_sync(0xffffffffu, incl, SCAN_WARPS - 1);
-        const T c0 = carry_in ? *carry_in : T(0);
-        const T block_excl = tile_prefix<T>(desc, tile, aggregate, c0);
+        const T c0 = carry_in ? *carry_in : init;
+        const T block_excl = tile_prefix<Op, T>(desc, tile, aggregate, c0);
         __syncwarp();
         // All 32 lanes take part in the shuffle; only 16 store.
         T wex = __shfl_up_sync(0xffffffffu, incl, 1);
-        if (lane == 0) wex = T(0);
-        if (lane < SCAN_WARPS) s_warp[lane] = add(block_excl, wex);
+        if (lane == 0) wex = Op::template identity<T>();
+        if (lane < SCAN_WARPS) s_warp[lane] = Op::template apply<T>(block_excl, wex);
     }
     __syncthreads();
     const T wbase = s_warp[warp];
@@ -178,26 +177,26 @@ scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in,
     if (vec_ok) {
 #pragma unroll
         for (int j = 0; j < SCAN_VECS; ++j) {
-            const T b = add(wbase, pre[j]);
+            const T b = Op::template apply<T>(wbase, pre[j]);
             T r[4];
             if (INCLUSIVE) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) r[k] = add(b, x[j][k]);
+                for (int k = 0; k < 4; ++k) r[k] = Op::template apply<T>(b, x[j][k]);
             } else {
                 r[0] = b;
 #pragma unroll
-                for (int k = 1; k < 4; ++k) r[k] = add(b, x[j][k - 1]);
+                for (int k = 1; k < 4; ++k) r[k] = Op::template apply<T>(b, x[j][k - 1]);
             }
             __stcs(reinterpret_cast<uint4*>(out + base + j * 128), *reinterpret_cast<const uint4*>(r));
         }
     } else {
 #pragma unroll
         for (int j = 0; j < SCAN_VECS; ++j) {
-            const T b = add(wbase, pre[j]);
+            const T b = Op::template apply<T>(wbase, pre[j]);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const uint64_t i = base + j * 128 + k;
-                if (i < n) out[i] = INCLUSIVE ? add(b, x[j][k]) : (k ? add(b, x[j][k - 1]) : b);
+                if (i < n) out[i] = INCLUSIVE ? Op::template apply<T>(b, x[j][k]) : (k ? Op::template apply<T>(b, x[j][k - 1]) : b);
             }
         }
     }
@@ -211,7 +210,7 @@ __global__ void lookback_tiles_kernel(const uint32_t* agg, uint32_t* excl_out, u
     __syncwarp();
     const int64_t tile = s_tile;
     const uint32_t a = agg[tile];
-    const uint32_t e = tile_prefix<uint32_t>(desc, tile, a, 0u);
+    const uint32_t e = tile_prefix<OpSum, uint32_t>(desc, tile, a, 0u);
     if (threadIdx.x == 0) {
         excl_out[tile] = e;
         incl_out[tile] = e + a;
@@ -219,7 +218,7 @@ __global__ void lookback_tiles_kernel(const uint32_t* agg, uint32_t* excl_out, u
 }
 
 __global__ void lookback_probe_kernel(const uint64_t* desc, int64_t tile, uint32_t* excl_out) {
-    const uint32_t e = lookback_warp<uint32_t>(desc, tile);
+    const uint32_t e = lookback_warp<OpSum, uint32_t>(desc, tile);
     if (threadIdx.x == 0) *excl_out = e;
 }
 
@@ -233,10 +232,11 @@ extern "C" size_t lcpp_scan_temp_bytes(int dtype, uint64_t n) {
     return SCAN_HDR + align_up(tiles * sizeof(uint64_t), 256);
 }
 
-extern "C" lcpp_status lcpp_scan_carry(int kind, int dtype, const void* in, void* out, uint64_t n,
-                                       const void* carry_in, void* temp, size_t temp_bytes,
-                                       void* stream) {
-    if ((kind != LCPP_SCAN_EXCLUSIVE && kind != LCPP_SCAN_INCLUSIVE) || (n && (!in || !out)))
+// Shared body of the scan entry points: op in {SUM, MIN, MAX}; the device
+// carry (multi-GPU) or, without one, the host value *init seeds tile 0.
+static lcpp_status scan_impl(int kind, int op, int dtype, const void* in, void* out, uint64_t n,
+                             const void* carry_in, const void* init, void* temp, size_t temp_bytes, void* stream) {
+    if ((kind != LCPP_SCAN_EXCLUSIVE && kind != LCPP_SCAN_INCLUSIVE) || op < 0 || op > 2 || (n && (!in || !out)))
         return LCPP_ERR_INVALID_ARG;
     const size_t need = lcpp_scan_temp_bytes(dtype, n);
     if (!need) return LCPP_ERR_INVALID_ARG;
@@ -251,24 +251,44 @@ extern "C" lcpp_status lcpp_scan_carry(int kind, int dtype, const void* in, void
     uint64_t* desc = (uint64_t*)((char*)temp + SCAN_HDR);
     if (cudaMemsetAsync(temp, 0, SCAN_HDR + (aligned ? desc_tiles : tiles) * sizeof(uint64_t), s) != cudaSuccess)
         return LCPP_ERR_CUDA;
-    auto go = [&](auto zero) -> lcpp_status {
+    auto go_op = [&](auto zero, auto opv) -> lcpp_status {
         using T = decltype(zero);
+        using Op = decltype(opv);
+        const T iv = init ? *(const T*)init : Op::template identity<T>();
+        const T* ci = (const T*)carry_in;
         ProfScope ps("scan", s);
         if (aligned)  // pipelined persistent kernel (scan_pipe.cu)
-            return scan_pipe_launch<T>(kind == LCPP_SCAN_INCLUSIVE, (const T*)in, (T*)out, n, (const T*)carry_in,
-                                       ticket, desc, s);
+            return scan_pipe_launch<Op, T>(kind == LCPP_SCAN_INCLUSIVE, (const T*)in, (T*)out, n, ci, iv, ticket,
+                                           desc, s);
         if (kind == LCPP_SCAN_INCLUSIVE)
-            scan_kernel<T, true><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, (const T*)carry_in, ticket, desc);
+            scan_kernel<Op, T, true><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, ci, iv, ticket, desc);
         else
-            scan_kernel<T, false><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, (const T*)carry_in, ticket, desc);
+            scan_kernel<Op, T, false><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, ci, iv, ticket, desc);
         count_launch();
         return check_launch();
+    };
+    auto go = [&](auto zero) -> lcpp_status {
+        switch (op) {
+            case LCPP_OP_SUM: return go_op(zero, OpSum{});
+            case LCPP_OP_MIN: return go_op(zero, OpMin{});
+            default: return go_op(zero, OpMax{});
+        }
     };
     switch (dtype) {
         case LCPP_I32: return go((int32_t)0);
         case LCPP_U32: return go((uint32_t)0);
         default: return go((float)0);
     }
+}
+
+extern "C" lcpp_status lcpp_scan_carry(int kind, int dtype, const void* in, void* out, uint64_t n,
+                                       const void* carry_in, void* temp, size_t temp_bytes, void* stream) {
+    return scan_impl(kind, LCPP_OP_SUM, dtype, in, out, n, carry_in, nullptr, temp, temp_bytes, stream);
+}
+
+extern "C" lcpp_status lcpp_scan_op(int kind, int op, int dtype, const void* in, void* out, uint64_t n,
+                                    const void* init, void* temp, size_t temp_bytes, void* stream) {
+    return scan_impl(kind, op, dtype, in, out, n, nullptr, init, temp, temp_bytes, stream);
 }
 
 extern "C" lcpp_status lcpp_scan(int kind, int dtype, const void* in, void* out, uint64_t n,

@@ -33,9 +33,9 @@ constexpr int SP_STAGES = 3;
 constexpr size_t SP_SMEM = SP_STAGES * (size_t)SP_STAGE_BYTES;
 static_assert(SP_TILE == SCAN_DESC_TILE, "descriptor array is sized for SCAN_DESC_TILE");
 
-template <typename T, bool INCLUSIVE>
+template <typename Op, typename T, bool INCLUSIVE>
 __global__ void __launch_bounds__(SP_THREADS, SP_CTAS_PER_SM)
-scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* carry_in,
+scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* carry_in, T init,
                  unsigned int* ticket, uint64_t* desc) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t s_bar[SP_STAGES];
@@ -47,7 +47,7 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint64_t full_tiles = n / SP_TILE;
     const uint32_t limit = g_spin_limit;
-    const T c0 = carry_in ? *carry_in : T(0);
+    const T c0 = carry_in ? *carry_in : init;
     const uint32_t woff = (uint32_t)warp * SP_WARP_ITEMS + lane * 4;
     uint32_t phase[SP_STAGES] = {};
 
@@ -68,28 +68,28 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
         } else {  // ragged last tile: guarded copy, zero fill
             for (int i = tid; i < SP_TILE; i += SP_THREADS) {
                 const uint64_t g = t * SP_TILE + i;
-                buf[i] = g < n ? in[g] : T(0);
+                buf[i] = g < n ? in[g] : Op::template identity<T>();
             }
             __syncthreads();
         }
-        T s = T(0);
+        T s = Op::template identity<T>();
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
             const uint4 q = *reinterpret_cast<const uint4*>(buf + woff + j * 128);
             const T* e = reinterpret_cast<const T*>(&q);
-            s = add(s, add(add(e[0], e[1]), add(e[2], e[3])));
+            s = Op::template apply<T>(s, Op::template apply<T>(Op::template apply<T>(e[0], e[1]), Op::template apply<T>(e[2], e[3])));
         }
-        s = warp_reduce<OpSum>(s);
+        s = warp_reduce<Op>(s);
         __syncthreads();  // earlier readers of s_warp are done
         if (lane == 0) s_warp[warp] = s;
         __syncthreads();
         if (warp == 0) {
-            T a = lane < SP_WARPS ? s_warp[lane] : T(0);
-            a = warp_reduce<OpSum>(a);
+            T a = lane < SP_WARPS ? s_warp[lane] : Op::template identity<T>();
+            a = warp_reduce<Op>(a);
             if (lane == 0) {
                 s_agg[st] = a;
                 if (t == 0)
-                    st_relaxed_u64(desc, ST_INCLUSIVE | to_bits<T>(add(c0, a)));
+                    st_relaxed_u64(desc, ST_INCLUSIVE | to_bits<T>(Op::template apply<T>(c0, a)));
                 else
                     st_relaxed_u64(desc + t, ST_PARTIAL | to_bits<T>(a));
             }
@@ -108,55 +108,55 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
             for (int k = 0; k < 4; ++k) x[j][k] = e[k];
         }
         T pre[SP_VECS];
-        T carry = T(0);
+        T carry = Op::template identity<T>();
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
 #pragma unroll
-            for (int k = 1; k < 4; ++k) x[j][k] = add(x[j][k - 1], x[j][k]);
+            for (int k = 1; k < 4; ++k) x[j][k] = Op::template apply<T>(x[j][k - 1], x[j][k]);
             T incl = x[j][3];
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const T y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl = add(y, incl);
+                if (lane >= o) incl = Op::template apply<T>(y, incl);
             }
             T excl = __shfl_up_sync(0xffffffffu, incl, 1);
-            if (lane == 0) excl = T(0);
-            pre[j] = add(carry, excl);
-            carry = add(carry, __shfl_sync(0xffffffffu, incl, 31));
+            if (lane == 0) excl = Op::template identity<T>();
+            pre[j] = Op::template apply<T>(carry, excl);
+            carry = Op::template apply<T>(carry, __shfl_sync(0xffffffffu, incl, 31));
         }
         __syncthreads();  // aggregate()'s readers of s_warp are done
         if (lane == 0) s_warp[warp] = carry;
         __syncthreads();
         if (warp == 0) {
-            T incl = lane < SP_WARPS ? s_warp[lane] : T(0);
+            T incl = lane < SP_WARPS ? s_warp[lane] : Op::template identity<T>();
 #pragma unroll
             for (int o = 1; o < SP_WARPS; o <<= 1) {
                 const T y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl = add(y, incl);
+                if (lane >= o) incl = Op::template apply<T>(y, incl);
             }
             T wex = __shfl_up_sync(0xffffffffu, incl, 1);
-            if (lane == 0) wex = T(0);
+            if (lane == 0) wex = Op::template identity<T>();
             T excl = c0;
             if (t != 0) {
-                excl = lookback_warp<T>(desc, (int64_t)t);
-                if (lane == 0) st_relaxed_u64(desc + t, ST_INCLUSIVE | to_bits<T>(add(excl, s_agg[st])));
+                excl = lookback_warp<Op, T>(desc, (int64_t)t);
+                if (lane == 0) st_relaxed_u64(desc + t, ST_INCLUSIVE | to_bits<T>(Op::template apply<T>(excl, s_agg[st])));
             }
-            if (lane < SP_WARPS) s_wex[lane] = add(excl, wex);
+            if (lane < SP_WARPS) s_wex[lane] = Op::template apply<T>(excl, wex);
         }
         __syncthreads();
         const T wbase = s_wex[warp];
         const bool full = t < full_tiles;
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
-            const T b = add(wbase, pre[j]);
+            const T b = Op::template apply<T>(wbase, pre[j]);
             T r[4];
             if (INCLUSIVE) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) r[k] = add(b, x[j][k]);
+                for (int k = 0; k < 4; ++k) r[k] = Op::template apply<T>(b, x[j][k]);
             } else {
                 r[0] = b;
 #pragma unroll
-                for (int k = 1; k < 4; ++k) r[k] = add(b, x[j][k - 1]);
+                for (int k = 1; k < 4; ++k) r[k] = Op::template apply<T>(b, x[j][k - 1]);
             }
             if (full) {
                 *reinterpret_cast<uint4*>(buf + woff + j * 128) = *reinterpret_cast<const uint4*>(r);
@@ -208,17 +208,17 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
     if (tid == 0) bulk_wait_all();
 }
 
-template <typename T>
-static lcpp_status scan_pipe_launch(bool inclusive, const T* in, T* out, uint64_t n, const T* carry_in,
+template <typename Op, typename T>
+static lcpp_status scan_pipe_launch(bool inclusive, const T* in, T* out, uint64_t n, const T* carry_in, T init,
                                     unsigned int* ticket, uint64_t* desc, cudaStream_t s) {
     const uint64_t tiles = ceil_div(n, SP_TILE);
     const DeviceInfo di = device_info();
     uint64_t grid = (uint64_t)di.sms * SP_CTAS_PER_SM;
     if (grid > ceil_div(tiles, 2)) grid = ceil_div(tiles, 2);
-    auto k = inclusive ? scan_pipe_kernel<T, true> : scan_pipe_kernel<T, false>;
+    auto k = inclusive ? scan_pipe_kernel<Op, T, true> : scan_pipe_kernel<Op, T, false>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SP_SMEM) != cudaSuccess)
         return LCPP_ERR_CUDA;
-    k<<<(unsigned)grid, SP_THREADS, SP_SMEM, s>>>(in, out, n, tiles, carry_in, ticket, desc);
+    k<<<(unsigned)grid, SP_THREADS, SP_SMEM, s>>>(in, out, n, tiles, carry_in, init, ticket, desc);
     count_launch();
     return check_launch();
 }

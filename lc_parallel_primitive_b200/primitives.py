@@ -209,6 +209,25 @@ class DeviceScan(_Module):
     def InclusiveSum(self, cmdlist, temp_storage, d_in, d_out, num_items):
         self._scan(L.SCAN_INCLUSIVE, cmdlist, temp_storage, d_in, d_out, num_items)
 
+    def _scan_op(self, kind, cmdlist, temp_storage, d_in, d_out, num_items, scan_op, initial_value):
+        import numpy as np
+
+        dt = lcpp_dtype(d_in)
+        npdt = {L.I32: np.int32, L.U32: np.uint32, L.F32: np.float32}[dt]
+        init = np.array([initial_value], dtype=npdt)
+        pin, pout, ptmp, nt = _ptr(d_in), _ptr(d_out), _ptr(temp_storage), _nbytes(temp_storage)
+        op = {"sum": L.OP_SUM, "min": L.OP_MIN, "max": L.OP_MAX}[scan_op] if isinstance(scan_op, str) else int(scan_op)
+        self._record(cmdlist,
+                     lambda s: L.lib().lcpp_scan_op(kind, op, dt, pin, pout, num_items, init.ctypes.data, ptmp, nt, s),
+                     "DeviceScan")
+
+    def ExclusiveScan(self, cmdlist, temp_storage, d_in, d_out, num_items, scan_op, initial_value):
+        """scan_op: "sum" | "min" | "max" (or LCPP_OP_*), as the reference's SumOp/MinOp/MaxOp."""
+        self._scan_op(L.SCAN_EXCLUSIVE, cmdlist, temp_storage, d_in, d_out, num_items, scan_op, initial_value)
+
+    def InclusiveScan(self, cmdlist, temp_storage, d_in, d_out, num_items, scan_op, initial_value):
+        self._scan_op(L.SCAN_INCLUSIVE, cmdlist, temp_storage, d_in, d_out, num_items, scan_op, initial_value)
+
 
 class DeviceRadixSort(_Module):
     @staticmethod

@@ -39,12 +39,13 @@ def lib():
         h.oracle_segment_reduce.argtypes = [i, i, vp, vp, u64, vp, vp]
         h.oracle_reduce_sum_mt.argtypes = [i, vp, u64, vp, i]
         h.oracle_arg_reduce.argtypes = [i, i, vp, u64, vp, vp]
+        h.oracle_scan_op.argtypes = [i, i, i, vp, u64, vp, vp]
         h.oracle_segment_arg_reduce.argtypes = [i, i, vp, vp, vp, u64, vp, vp]
         h.oracle_scan_mt.argtypes = [i, i, vp, vp, u64, i]
         h.oracle_segment_reduce_mt.argtypes = [i, i, vp, vp, u64, vp, vp, i]
         for f in ("oracle_reduce", "oracle_scan", "oracle_abs_prefix_f32", "oracle_radix_sort",
                   "oracle_segment_reduce", "oracle_reduce_sum_mt", "oracle_scan_mt",
-                  "oracle_segment_reduce_mt", "oracle_arg_reduce", "oracle_segment_arg_reduce"):
+                  "oracle_segment_reduce_mt", "oracle_arg_reduce", "oracle_segment_arg_reduce", "oracle_scan_op"):
             getattr(h, f).restype = i
         _lib = h
     return _lib
@@ -147,3 +148,12 @@ def segment_arg_reduce(op: int, x: np.ndarray, begin: np.ndarray, end: np.ndarra
     _ok(lib().oracle_segment_arg_reduce(op, _dt(x), _p(x), _p(v), _p(i), begin.size, _p(begin), _p(end)),
         "segment_arg_reduce")
     return v, i
+
+
+def scan_op(inclusive: bool, op: int, x: np.ndarray, init) -> np.ndarray:
+    """Scan with SUM/MIN/MAX and an initial value, in the element type."""
+    x = np.ascontiguousarray(x)
+    iv = np.array([init], dtype=x.dtype)
+    out = np.empty_like(x)
+    _ok(lib().oracle_scan_op(int(inclusive), op, _dt(x), _p(x), x.size, _p(iv), _p(out)), "scan_op")
+    return out

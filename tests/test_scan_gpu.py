@@ -73,3 +73,45 @@ def test_config2_inclusive_f32_full(cuda):
     x = G.f32_normal(1 << 28, seed=1, stream=5)
     got = abi_scan(True, x)
     assert_float_sum_close(got, oracle.scan(True, x), oracle.abs_prefix(x))
+
+
+@pytest.mark.parametrize("inclusive", [False, True])
+@pytest.mark.parametrize("op", [1, 2])
+@pytest.mark.parametrize("dtype", [np.int32, np.uint32, np.float32])
+def test_min_max_scan_with_init(cuda, inclusive, op, dtype):
+    # DeviceScan::ExclusiveScan / InclusiveScan with MinOp / MaxOp and an initial value.
+    import torch
+    from lc_parallel_primitive_b200 import _lib as L
+    from tests.helpers import NP2LCPP, empty_dev, stream, temp, to_dev
+
+    lib = L.lib()
+    for k, n in enumerate([1, 1000, 8193, 100003, (1 << 21) + 5]):
+        x = G.u32(n, seed=500 + k).view(np.int32).astype(dtype) if dtype != np.uint32 else G.u32(n, seed=500 + k)
+        init = np.array([x[n // 2]], dtype=dtype)  # a value inside the range
+        dt = NP2LCPP[np.dtype(dtype)]
+        d = to_dev(x, k % 2)
+        out = empty_dev(n, dtype, k % 2)
+        tb = lib.lcpp_scan_temp_bytes(dt, n)
+        t = temp(tb)
+        L.check(lib.lcpp_scan_op(int(inclusive), op, dt, d.data_ptr(), out.data_ptr(), n, init.ctypes.data,
+                                 t.data_ptr(), tb, stream()))
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), oracle.scan_op(inclusive, op, x, init[0])), n
+
+
+def test_sum_scan_with_init(cuda):
+    import torch
+    from lc_parallel_primitive_b200 import _lib as L
+    from tests.helpers import empty_dev, stream, temp, to_dev
+
+    lib = L.lib()
+    x = G.u32(300007, seed=77)
+    init = np.array([123456789], dtype=np.uint32)
+    for inclusive in (False, True):
+        d, out = to_dev(x), empty_dev(x.size, np.uint32)
+        tb = lib.lcpp_scan_temp_bytes(L.U32, x.size)
+        t = temp(tb)
+        L.check(lib.lcpp_scan_op(int(inclusive), 0, L.U32, d.data_ptr(), out.data_ptr(), x.size, init.ctypes.data,
+                                 t.data_ptr(), tb, stream()))
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), oracle.scan_op(inclusive, 0, x, init[0]))
