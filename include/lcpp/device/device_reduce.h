@@ -1,7 +1,8 @@
 /*
  * DeviceReduce — same class template, methods and argument meaning as the
- * reference (src/lcpp/device/device_reduce.h:41-185); the work runs in the
- * sm_100a kernels of liblcpp_b200.so through lcpp_reduce().
+ * reference (src/lcpp/device/device_reduce.h:41-325); the work runs in the
+ * sm_100a kernels of liblcpp_b200.so through lcpp_reduce(), lcpp_arg_reduce()
+ * and lcpp_reduce_by_key().
  */
 #pragma once
 #include "lcpp/runtime/core.h"
@@ -60,6 +61,27 @@ class DeviceReduce : public LuisaModule {
     void ArgMax(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
                 BufferView<Type4Byte> d_out, BufferView<uint> d_index_out, size_t num_item) {
         record_arg(cmdlist, LCPP_OP_MAX, temp_storage, d_in, d_out, d_index_out, num_item);
+    }
+
+    // Reference: device_reduce.h:110-125 (temp size), 277-325.  ReduceOp must
+    // be SumOp, MinOp or MaxOp; g_num_runs_out receives the number of runs.
+    template <NumericT KeyType, NumericT ValueType>
+    static size_t GetReduceByKeyTempStorageBytes(size_t num_elements) {
+        return lcpp_reduce_by_key_temp_bytes(lcpp_dtype_of<KeyType>(), lcpp_dtype_of<ValueType>(), num_elements);
+    }
+    template <NumericT KeyType, NumericT ValueType, typename ReduceOp>
+    void ReduceByKey(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<KeyType> d_keys_in,
+                     BufferView<ValueType> d_values_in, BufferView<KeyType> d_unique_out,
+                     BufferView<ValueType> g_aggregates_out, BufferView<uint> g_num_runs_out, ReduceOp,
+                     size_t num_elements) {
+        const int op = ReduceOp::lcpp_op;
+        cmdlist << [=](cudaStream_t s) {
+            return lcpp_reduce_by_key(op, lcpp_dtype_of<KeyType>(), lcpp_dtype_of<ValueType>(), d_keys_in.data(),
+                                      d_values_in.data(), d_unique_out.data(), g_aggregates_out.data(),
+                                      g_num_runs_out.data(), num_elements, temp_storage.data(),
+                                      temp_storage.size_bytes(), s);
+        };
+        lcpp_check(cmdlist, m_debug_stream);
     }
 
   private:

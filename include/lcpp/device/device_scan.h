@@ -1,8 +1,10 @@
 /*
  * DeviceScan — same class template, methods and argument meaning as the
- * reference (src/lcpp/device/device_scan.h:33-204); single-pass decoupled
- * look-back scan in liblcpp_b200.so through lcpp_scan().  Element types: the
- * reference's Type4Byte (int32, uint32, float).
+ * reference (src/lcpp/device/device_scan.h:33-345); single-pass decoupled
+ * look-back scans in liblcpp_b200.so through lcpp_scan*() and
+ * lcpp_scan_by_key().  Element types of the plain scans: the reference's
+ * Type4Byte (int32, uint32, float); ScanByKey takes any of the six numeric
+ * types for keys and values.
  */
 #pragma once
 #include "lcpp/runtime/core.h"
@@ -47,7 +49,49 @@ class DeviceScan : public LuisaModule {
         record_op(cmdlist, LCPP_SCAN_INCLUSIVE, ScanOp::lcpp_op, temp_storage, d_in, d_out, num_items, initial_value);
     }
 
+    // Reference: device_scan.h:93-107 (temp size), 206-345.  Segments are runs
+    // of equal consecutive keys; ScanOp must be SumOp, MinOp or MaxOp.
+    template <NumericT KeyType, NumericT ValueType>
+    static size_t GetScanByKeyTempStorageBytes(size_t num_items) {
+        return lcpp_scan_by_key_temp_bytes(lcpp_dtype_of<KeyType>(), lcpp_dtype_of<ValueType>(), num_items);
+    }
+    template <NumericT KeyType, NumericT ValueType, typename ScanOp>
+    void ExclusiveScanByKey(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<KeyType> d_keys_in,
+                            BufferView<ValueType> d_values_in, BufferView<ValueType> d_values_out, ScanOp,
+                            size_t num_items, ValueType initial_value) {
+        record_by_key(cmdlist, LCPP_SCAN_EXCLUSIVE, ScanOp::lcpp_op, temp_storage, d_keys_in, d_values_in,
+                      d_values_out, num_items, initial_value);
+    }
+    template <NumericT KeyType, NumericT ValueType, typename ScanOp>
+    void InclusiveScanByKey(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<KeyType> d_keys_in,
+                            BufferView<ValueType> d_values_in, BufferView<ValueType> d_values_out, ScanOp,
+                            size_t num_items, ValueType initial_value) {
+        record_by_key(cmdlist, LCPP_SCAN_INCLUSIVE, ScanOp::lcpp_op, temp_storage, d_keys_in, d_values_in,
+                      d_values_out, num_items, initial_value);
+    }
+    template <NumericT Type4Byte>
+    void ExclusiveSumByKey(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_keys_in,
+                           BufferView<Type4Byte> d_values_in, BufferView<Type4Byte> d_values_out, size_t num_items) {
+        record_by_key(cmdlist, LCPP_SCAN_EXCLUSIVE, LCPP_OP_SUM, temp_storage, d_keys_in, d_values_in, d_values_out,
+                      num_items, Type4Byte(0));
+    }
+    template <NumericT Type4Byte>
+    void InclusiveSumByKey(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_keys_in,
+                           BufferView<Type4Byte> d_values_in, BufferView<Type4Byte> d_values_out, size_t num_items) {
+        record_by_key(cmdlist, LCPP_SCAN_INCLUSIVE, LCPP_OP_SUM, temp_storage, d_keys_in, d_values_in, d_values_out,
+                      num_items, Type4Byte(0));
+    }
+
   private:
+    template <typename K, typename T>
+    void record_by_key(CommandList& cmdlist, int kind, int op, BufferView<uint> temp, BufferView<K> keys,
+                       BufferView<T> in, BufferView<T> out, size_t n, T init) {
+        cmdlist << [=](cudaStream_t s) {
+            return lcpp_scan_by_key(kind, op, lcpp_dtype_of<K>(), lcpp_dtype_of<T>(), keys.data(), in.data(),
+                                    out.data(), n, &init, temp.data(), temp.size_bytes(), s);
+        };
+        lcpp_check(cmdlist, m_debug_stream);
+    }
     template <typename T>
     void record_op(CommandList& cmdlist, int kind, int op, BufferView<uint> temp, BufferView<T> in,
                    BufferView<T> out, size_t n, T init) {

@@ -189,6 +189,34 @@ lcpp_status lcpp_segment_arg_reduce_fixed(int op, int dtype, const void* in, voi
                                           uint32_t* out_index, uint64_t num_segments,
                                           uint64_t segment_size, void* stream);
 
+/* ---- ScanByKey / ReduceByKey ------------------------------------------
+ * Segments are runs of equal consecutive keys (a new one starts where
+ * keys[i] != keys[i-1]; float keys compare by value).  op in {SUM, MIN, MAX};
+ * key_dtype and value_dtype: any of I32 U32 F32 I64 U64 F64; n < 2^32.
+ *
+ * lcpp_scan_by_key: per-segment scan of values_in, seeded by the HOST value
+ * *init (NULL = the op's identity): exclusive out[i] = init at a segment head,
+ * op(v[head] .. v[i-1], init) elsewhere; inclusive out[i] =
+ * op(v[head] .. v[i], init).  values_out may equal values_in.  Replaces
+ * DeviceScan::ExclusiveScanByKey / InclusiveScanByKey / ExclusiveSumByKey /
+ * InclusiveSumByKey and GetScanByKeyTempStorageBytes (device_scan.h:93-107,
+ * 206-345).
+ *
+ * lcpp_reduce_by_key: one output per run: unique_out[r] = key of the run's
+ * last item, aggregates_out[r] = op over the run's values, *num_runs_out
+ * (device) = number of runs (0 for n == 0).  Replaces DeviceReduce::
+ * ReduceByKey and GetReduceByKeyTempStorageBytes (device_reduce.h:110-125,
+ * 277-325). */
+size_t      lcpp_scan_by_key_temp_bytes(int key_dtype, int value_dtype, uint64_t n);
+lcpp_status lcpp_scan_by_key(int kind, int op, int key_dtype, int value_dtype, const void* keys,
+                             const void* values_in, void* values_out, uint64_t n, const void* init,
+                             void* temp, size_t temp_bytes, void* stream);
+size_t      lcpp_reduce_by_key_temp_bytes(int key_dtype, int value_dtype, uint64_t n);
+lcpp_status lcpp_reduce_by_key(int op, int key_dtype, int value_dtype, const void* keys_in,
+                               const void* values_in, void* unique_out, void* aggregates_out,
+                               uint32_t* num_runs_out, uint64_t n, void* temp, size_t temp_bytes,
+                               void* stream);
+
 /* ---- Device error word --------------------------------------------------
  * Synchronizes `stream`, returns the first device-side error latched since
  * the last call on the current device (LCPP_OK if none) and clears it.  The

@@ -51,6 +51,10 @@ SIGNATURES = {
     "lcpp_arg_reduce": (_i, [_i, _i, _vp, _vp, _vp, _u64, _vp, _sz, _vp]),
     "lcpp_segment_arg_reduce": (_i, [_i, _i, _vp, _vp, _vp, _u64, _vp, _vp, _vp]),
     "lcpp_segment_arg_reduce_fixed": (_i, [_i, _i, _vp, _vp, _vp, _u64, _u64, _vp]),
+    "lcpp_scan_by_key_temp_bytes": (_sz, [_i, _i, _u64]),
+    "lcpp_scan_by_key": (_i, [_i, _i, _i, _i, _vp, _vp, _vp, _u64, _vp, _vp, _sz, _vp]),
+    "lcpp_reduce_by_key_temp_bytes": (_sz, [_i, _i, _u64]),
+    "lcpp_reduce_by_key": (_i, [_i, _i, _i, _vp, _vp, _vp, _vp, _vp, _u64, _vp, _sz, _vp]),
     "lcpp_last_device_error": (_i, [_vp]),
     "lcpp_lookback_temp_bytes": (_sz, [_u64]),
     "lcpp_lookback_tiles": (_i, [_vp, _vp, _vp, _u64, _vp, _sz, _vp]),

@@ -8,3 +8,4 @@
 #include "segment_reduce.cu"
 #include "arg_reduce.cu"
 #include "scan_noalloc.cu"
+#include "by_key.cu"

@@ -3,8 +3,8 @@
 Same class names, method names, argument order and meaning as the reference's
 C++ templates (namespace luisa::parallel_primitive):
 
-  DeviceReduce        src/lcpp/device/device_reduce.h:41-185
-  DeviceScan          src/lcpp/device/device_scan.h:33-204
+  DeviceReduce        src/lcpp/device/device_reduce.h:41-325 (incl. ArgMin/ArgMax, ReduceByKey)
+  DeviceScan          src/lcpp/device/device_scan.h:33-345 (incl. ScanByKey)
   DeviceRadixSort     src/lcpp/device/device_radix_sort.h:37-184
   DeviceSegmentReduce src/lcpp/device/device_segment_reduce.h:26-194
 
@@ -43,6 +43,20 @@ def lcpp_dtype(t) -> int:
         return _DTYPES[dt]
     except KeyError:
         raise TypeError(f"unsupported element type {dt}") from None
+
+
+_NP = {L.I32: "int32", L.U32: "uint32", L.F32: "float32", L.I64: "int64", L.U64: "uint64", L.F64: "float64"}
+
+
+def _host_scalar(value, dt):
+    """One element of lcpp dtype `dt` in host memory (kept alive by the caller)."""
+    import numpy as np
+
+    return np.array([value], dtype=_NP[dt])
+
+
+def _op_code(op) -> int:
+    return {"sum": L.OP_SUM, "min": L.OP_MIN, "max": L.OP_MAX}[op] if isinstance(op, str) else int(op)
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -189,6 +203,29 @@ class DeviceReduce(_Module):
         self._arg(cmdlist, temp_storage, d_in, d_out, d_index_out, num_item, L.OP_MAX)
 
 
+    # ---- ReduceByKey (device_reduce.h:110-125, 277-325) ---------------------
+    @staticmethod
+    def GetReduceByKeyTempStorageBytes(num_elements: int, key_dtype=torch.int32, value_dtype=torch.int32) -> int:
+        return int(L.lib().lcpp_reduce_by_key_temp_bytes(lcpp_dtype(key_dtype), lcpp_dtype(value_dtype),
+                                                         num_elements))
+
+    def ReduceByKey(self, cmdlist, temp_storage, d_keys_in, d_values_in, d_unique_out, g_aggregates_out,
+                    g_num_runs_out, reduce_op, num_elements):
+        """reduce_op: "sum" | "min" | "max" (or LCPP_OP_*); g_num_runs_out: one uint32 on the device."""
+        kdt, vdt = lcpp_dtype(d_keys_in), lcpp_dtype(d_values_in)
+        if lcpp_dtype(d_unique_out) != kdt or lcpp_dtype(g_aggregates_out) != vdt:
+            raise TypeError("output element types must match the key / value types")
+        if g_num_runs_out.dtype not in (torch.uint32, torch.int32):
+            raise TypeError("g_num_runs_out must hold 32-bit unsigned integers")
+        op = _op_code(reduce_op)
+        pk, pv, pu, pa, pn = (_ptr(d_keys_in), _ptr(d_values_in), _ptr(d_unique_out), _ptr(g_aggregates_out),
+                              _ptr(g_num_runs_out))
+        ptmp, nt = _ptr(temp_storage), _nbytes(temp_storage)
+        self._record(cmdlist,
+                     lambda s: L.lib().lcpp_reduce_by_key(op, kdt, vdt, pk, pv, pu, pa, pn, num_elements, ptmp, nt, s),
+                     "DeviceReduce.ReduceByKey")
+
+
 class DeviceScan(_Module):
     @staticmethod
     def GetTempStorageBytes(num_items: int, dtype=torch.uint32) -> int:
@@ -227,6 +264,42 @@ class DeviceScan(_Module):
 
     def InclusiveScan(self, cmdlist, temp_storage, d_in, d_out, num_items, scan_op, initial_value):
         self._scan_op(L.SCAN_INCLUSIVE, cmdlist, temp_storage, d_in, d_out, num_items, scan_op, initial_value)
+
+
+    # ---- ScanByKey (device_scan.h:93-107, 206-345) -------------------------
+    @staticmethod
+    def GetScanByKeyTempStorageBytes(num_items: int, key_dtype=torch.int32, value_dtype=torch.int32) -> int:
+        return int(L.lib().lcpp_scan_by_key_temp_bytes(lcpp_dtype(key_dtype), lcpp_dtype(value_dtype), num_items))
+
+    def _scan_by_key(self, kind, cmdlist, temp_storage, d_keys_in, d_values_in, d_values_out, scan_op,
+                     num_items, initial_value):
+        kdt, vdt = lcpp_dtype(d_keys_in), lcpp_dtype(d_values_in)
+        if lcpp_dtype(d_values_out) != vdt:
+            raise TypeError("d_values_in and d_values_out must have the same element type")
+        init = _host_scalar(initial_value, vdt)
+        op = _op_code(scan_op)
+        pk, pv, po = _ptr(d_keys_in), _ptr(d_values_in), _ptr(d_values_out)
+        ptmp, nt = _ptr(temp_storage), _nbytes(temp_storage)
+        self._record(cmdlist,
+                     lambda s: L.lib().lcpp_scan_by_key(kind, op, kdt, vdt, pk, pv, po, num_items,
+                                                        init.ctypes.data, ptmp, nt, s),
+                     "DeviceScan.ScanByKey")
+
+    def ExclusiveScanByKey(self, cmdlist, temp_storage, d_keys_in, d_values_in, d_values_out, scan_op,
+                           num_items, initial_value):
+        self._scan_by_key(L.SCAN_EXCLUSIVE, cmdlist, temp_storage, d_keys_in, d_values_in, d_values_out,
+                          scan_op, num_items, initial_value)
+
+    def InclusiveScanByKey(self, cmdlist, temp_storage, d_keys_in, d_values_in, d_values_out, scan_op,
+                           num_items, initial_value):
+        self._scan_by_key(L.SCAN_INCLUSIVE, cmdlist, temp_storage, d_keys_in, d_values_in, d_values_out,
+                          scan_op, num_items, initial_value)
+
+    def ExclusiveSumByKey(self, cmdlist, temp_storage, d_keys_in, d_values_in, d_values_out, num_items):
+        self.ExclusiveScanByKey(cmdlist, temp_storage, d_keys_in, d_values_in, d_values_out, "sum", num_items, 0)
+
+    def InclusiveSumByKey(self, cmdlist, temp_storage, d_keys_in, d_values_in, d_values_out, num_items):
+        self.InclusiveScanByKey(cmdlist, temp_storage, d_keys_in, d_values_in, d_values_out, "sum", num_items, 0)
 
 
 class DeviceRadixSort(_Module):

@@ -43,9 +43,12 @@ def lib():
         h.oracle_segment_arg_reduce.argtypes = [i, i, vp, vp, vp, u64, vp, vp]
         h.oracle_scan_mt.argtypes = [i, i, vp, vp, u64, i]
         h.oracle_segment_reduce_mt.argtypes = [i, i, vp, vp, u64, vp, vp, i]
+        h.oracle_scan_by_key.argtypes = [i, i, i, i, vp, vp, u64, vp, vp]
+        h.oracle_reduce_by_key.argtypes = [i, i, i, vp, vp, u64, vp, vp, vp]
         for f in ("oracle_reduce", "oracle_scan", "oracle_abs_prefix_f32", "oracle_radix_sort",
                   "oracle_segment_reduce", "oracle_reduce_sum_mt", "oracle_scan_mt",
-                  "oracle_segment_reduce_mt", "oracle_arg_reduce", "oracle_segment_arg_reduce", "oracle_scan_op"):
+                  "oracle_segment_reduce_mt", "oracle_arg_reduce", "oracle_segment_arg_reduce", "oracle_scan_op",
+                  "oracle_scan_by_key", "oracle_reduce_by_key"):
             getattr(h, f).restype = i
         _lib = h
     return _lib
@@ -157,3 +160,46 @@ def scan_op(inclusive: bool, op: int, x: np.ndarray, init) -> np.ndarray:
     out = np.empty_like(x)
     _ok(lib().oracle_scan_op(int(inclusive), op, _dt(x), _p(x), x.size, _p(iv), _p(out)), "scan_op")
     return out
+
+
+def _limits(dt):
+    """(lowest, max) of a dtype, the identities of Max / Min."""
+    dt = np.dtype(dt)
+    if dt.kind == "f":
+        fi = np.finfo(dt)
+        return fi.min, fi.max
+    ii = np.iinfo(dt)
+    return ii.min, ii.max
+
+
+def _out_dtype(x: np.ndarray):
+    return np.dtype(np.float64) if x.dtype.kind == "f" else x.dtype
+
+
+def scan_by_key(inclusive: bool, op: int, keys: np.ndarray, values: np.ndarray, init=None) -> np.ndarray:
+    """Per-segment scan (segments = runs of equal keys).  Integer values: exact,
+    in the value dtype.  Float values: fp64 results."""
+    keys, values = np.ascontiguousarray(keys), np.ascontiguousarray(values)
+    if keys.size != values.size:
+        raise ValueError("keys and values differ in length")
+    if init is None:
+        init = {OP_SUM: 0, OP_MIN: _limits(values.dtype)[1], OP_MAX: _limits(values.dtype)[0]}[op]
+    iv = np.array([init], dtype=values.dtype)
+    out = np.empty(values.size, dtype=_out_dtype(values))
+    _ok(lib().oracle_scan_by_key(int(inclusive), op, _dt(keys), _dt(values), _p(keys), _p(values), values.size,
+                                 _p(iv), _p(out)), "scan_by_key")
+    return out
+
+
+def reduce_by_key(op: int, keys: np.ndarray, values: np.ndarray):
+    """(unique_keys, aggregates, num_runs); float aggregates in fp64."""
+    keys, values = np.ascontiguousarray(keys), np.ascontiguousarray(values)
+    if keys.size != values.size:
+        raise ValueError("keys and values differ in length")
+    uk = np.empty(max(keys.size, 1), dtype=keys.dtype)
+    agg = np.empty(max(keys.size, 1), dtype=_out_dtype(values))
+    nr = np.zeros(1, dtype=np.uint32)
+    _ok(lib().oracle_reduce_by_key(op, _dt(keys), _dt(values), _p(keys), _p(values), keys.size, _p(uk),
+                                   _p(agg), _p(nr)), "reduce_by_key")
+    r = int(nr[0])
+    return uk[:r], agg[:r], r

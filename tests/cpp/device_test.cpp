@@ -267,6 +267,55 @@ int main(int argc, char* argv[]) {
         }
     }
 
+    // ---- device_scan_test.cpp:111-167 (ExclusiveSumByKey) / device_reduce_test.cpp:229-295 --
+    {
+        DeviceScan<> scanner;
+        scanner.create(device, &stream);
+        for (int i = 5; i < 24; i += 6) {
+            const uint n = 1u << i;
+            const int per = 100;
+            std::vector<int32> ones(n, 1), keys(n);
+            for (uint j = 0; j < n; j++) keys[j] = (int32)(j / per);
+            auto kb = device.create_buffer<int32>(n), vb = device.create_buffer<int32>(n), ob = device.create_buffer<int32>(n);
+            stream << kb.copy_from(keys.data()) << vb.copy_from(ones.data()) << synchronize();
+            auto temp = device.create_buffer<uint>(
+                bytes_to_uint_count(DeviceScan<>::GetScanByKeyTempStorageBytes<int32, int32>(n)));
+            CommandList cmdlist;
+            scanner.ExclusiveSumByKey(cmdlist, temp.view(), kb.view(), vb.view(), ob.view(), kb.size());
+            std::vector<int32> res(n);
+            stream << cmdlist.commit() << synchronize() << ob.copy_to(res.data()) << synchronize();
+            int bad = 0;
+            for (uint j = 0; j < n; j++) bad += res[j] != (int32)(j % per);
+            EXPECT(bad == 0, "exclusive_sum_by_key n=%u: %d wrong", n, bad);
+        }
+        const int N = 1 << 12, per = 100, S = (N + per - 1) / per;
+        std::vector<int32> input(N), keys(N);
+        std::iota(input.begin(), input.end(), 0);
+        std::mt19937 rng(114521);
+        std::shuffle(input.begin(), input.end(), rng);
+        for (int j = 0; j < N; j++) keys[j] = j / per;
+        DeviceReduce<> reducer;
+        reducer.create(device, &stream);
+        auto kb = device.create_buffer<int32>(N), vb = device.create_buffer<int32>(N);
+        auto ub = device.create_buffer<int32>(S), ab = device.create_buffer<int32>(S);
+        auto rb = device.create_buffer<uint>(1);
+        stream << kb.copy_from(keys.data()) << vb.copy_from(input.data()) << synchronize();
+        auto temp = device.create_buffer<uint>(
+            bytes_to_uint_count(DeviceReduce<>::GetReduceByKeyTempStorageBytes<int32, int32>(N)));
+        CommandList cmdlist;
+        reducer.ReduceByKey(cmdlist, temp.view(), kb.view(), vb.view(), ub.view(), ab.view(), rb.view(), SumOp{},
+                            kb.size());
+        std::vector<int32> uk(S), agg(S);
+        std::vector<uint> runs(1);
+        stream << cmdlist.commit() << synchronize() << ub.copy_to(uk.data()) << ab.copy_to(agg.data())
+               << rb.copy_to(runs.data()) << synchronize();
+        EXPECT(runs[0] == (uint)S, "reduce_by_key runs %u", runs[0]);
+        for (int s = 0; s < S; s++) {
+            int want = std::accumulate(input.begin() + s * per, input.begin() + std::min((s + 1) * per, N), 0);
+            EXPECT(agg[s] == want && uk[s] == s, "reduce_by_key run %d", s);
+        }
+    }
+
     EXPECT(stream.last_status() == 0, "stream status %d", stream.last_status());
     std::printf("%s: %d failure(s)\n", g_failures ? "FAILED" : "OK", g_failures);
     return g_failures ? 1 : 0;

@@ -120,6 +120,37 @@ int main(int argc, char** argv) {
         for (int s = 0; s < N / per; s++) sums[s] = std::accumulate(in.begin() + s * per, in.begin() + (s + 1) * per, 0);
         dump("input", "i32", in);
         dump("expected", "i32", sums);
+    } else if (c == "reduce_by_key") {
+        // tests/device_reduce_test.cpp:54-62, 229-295: shuffled iota(4096),
+        // keys i / 100, expected per-run std:: sums and the run count.
+        const int N = 1 << 12, per = 100;
+        std::vector<int32_t> in(N), keys(N);
+        for (int i = 0; i < N; i++) in[i] = i;
+        std::mt19937 rng(114521);
+        std::shuffle(in.begin(), in.end(), rng);
+        for (int i = 0; i < N; i++) keys[i] = i / per;
+        const int S = (N + per - 1) / per;
+        std::vector<int32_t> sums(S), uk(S);
+        for (int s = 0; s < S; s++) {
+            sums[s] = std::accumulate(in.begin() + s * per, in.begin() + std::min((s + 1) * per, N), 0);
+            uk[s] = s;
+        }
+        dump("keys", "i32", keys);
+        dump("values", "i32", in);
+        dump("unique_expected", "i32", uk);
+        dump("aggregates_expected", "i32", sums);
+        dump("num_runs_expected", "u32", std::vector<uint32_t>{(uint32_t)S});
+    } else if (c == "exclusive_sum_by_key") {
+        // tests/device_scan_test.cpp:111-167 (one array size n): values all 1,
+        // keys i / 100, expected std::exclusive_scan of each segment.
+        const int N = (int)n, per = 100;
+        std::vector<int32_t> in(N, 1), keys(N), ex(N);
+        for (int i = 0; i < N; i++) keys[i] = i / per;
+        for (int b = 0; b < N; b += per)
+            std::exclusive_scan(in.begin() + b, in.begin() + std::min(b + per, N), ex.begin() + b, 0);
+        dump("keys", "i32", keys);
+        dump("values", "i32", in);
+        dump("expected", "i32", ex);
     } else {
         std::fprintf(stderr, "unknown case %s\n", c.c_str());
         return 1;

@@ -144,6 +144,48 @@ def abi_segment_reduce_fixed(op, x_np, num_segments, seg_size):
     return to_host(out)
 
 
+def abi_scan_by_key(inclusive, op, keys_np, values_np, init=None, offset_elems=0, in_place=False):
+    import torch
+
+    lib = L.lib()
+    kdt, vdt = NP2LCPP[keys_np.dtype], NP2LCPP[values_np.dtype]
+    n = values_np.size
+    k = to_dev(keys_np, offset_elems)
+    v = to_dev(values_np, offset_elems)
+    out = v if in_place else empty_dev(n, values_np.dtype, offset_elems)
+    tb = lib.lcpp_scan_by_key_temp_bytes(kdt, vdt, n)
+    t = temp(tb)
+    iv = None if init is None else np.array([init], dtype=values_np.dtype)
+    L.check(lib.lcpp_scan_by_key(L.SCAN_INCLUSIVE if inclusive else L.SCAN_EXCLUSIVE, op, kdt, vdt,
+                                 k.data_ptr(), v.data_ptr(), out.data_ptr(), n,
+                                 None if iv is None else iv.ctypes.data, t.data_ptr(), tb, stream()))
+    torch.cuda.synchronize()
+    L.check(lib.lcpp_last_device_error(stream()))
+    return to_host(out)
+
+
+def abi_reduce_by_key(op, keys_np, values_np, offset_elems=0):
+    """(unique_keys, aggregates, num_runs) from the device."""
+    import torch
+
+    lib = L.lib()
+    kdt, vdt = NP2LCPP[keys_np.dtype], NP2LCPP[values_np.dtype]
+    n = values_np.size
+    k = to_dev(keys_np, offset_elems)
+    v = to_dev(values_np, offset_elems)
+    uk = empty_dev(max(n, 1), keys_np.dtype)
+    agg = empty_dev(max(n, 1), values_np.dtype)
+    nr = torch.full((1,), 0xDEAD, dtype=torch.int32, device="cuda")
+    tb = lib.lcpp_reduce_by_key_temp_bytes(kdt, vdt, n)
+    t = temp(tb)
+    L.check(lib.lcpp_reduce_by_key(op, kdt, vdt, k.data_ptr(), v.data_ptr(), uk.data_ptr(), agg.data_ptr(),
+                                   nr.data_ptr(), n, t.data_ptr(), tb, stream()))
+    torch.cuda.synchronize()
+    L.check(lib.lcpp_last_device_error(stream()))
+    r = int(nr.cpu().numpy().view(np.uint32)[0])
+    return to_host(uk)[:r], to_host(agg)[:r], r
+
+
 # ---- reference-test regeneration (tests/golden/refgen.cpp) -----------------
 def refgen(case: str, n: int = 0) -> dict:
     from oracle.build import build_refgen
