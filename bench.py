@@ -436,8 +436,8 @@ def run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_k
 
 
 def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier, shrink=0):
-    """Scan (config 2), reduce (config 1) and segment reduce (config 4), each
-    timed with CUDA events; GB/s from algorithmic bytes."""
+    """Scan (config 2), reduce (config 1), segment reduce (config 4), scan-by-key
+    and reduce-by-key, each timed with CUDA events; GB/s from algorithmic bytes."""
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     out = {}
@@ -514,6 +514,29 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
     byts = 4 * N + 4 * (S + 1) + 4 * S  # values + CSR offsets + outputs
     out[f"segment_sum_f32_2p{27 - shrink}_2p{20 - shrink}"] = {"ms": ms, "GB/s": byts / ms / 1e6,
                                                               "frac": byts / ms / 1e6 / peak, **kern}
+
+    # scan-by-key / reduce-by-key: 2^28 int32 keys in runs of mean length 100, int32 values
+    n = 1 << (28 - shrink)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    keys = torch.cumsum((torch.rand(n, device=dev, generator=gen) < 0.01).to(torch.int32), 0, dtype=torch.int32)
+    vals = torch.from_numpy(G.i32_range(n, -1000, 1000, seed=1, stream=12)).to(dev)
+    outv = torch.empty_like(vals)
+    uk = torch.empty_like(keys)
+    nr = torch.empty(1, dtype=torch.int32, device=dev)
+    tb = lib.lcpp_scan_by_key_temp_bytes(L.I32, L.I32, n)
+    t = torch.empty(tb, dtype=torch.uint8, device=dev)
+    ms = timeit(lambda: L.check(lib.lcpp_scan_by_key(0, 0, L.I32, L.I32, keys.data_ptr(), vals.data_ptr(),
+                                                     outv.data_ptr(), n, None, t.data_ptr(), tb, sh)), 20)
+    out[f"exclusive_sum_by_key_i32_2p{28 - shrink}"] = {"ms": ms, "GB/s": 12 * n / ms / 1e6,
+                                                         "frac": 12 * n / ms / 1e6 / peak}
+    ms = timeit(lambda: L.check(lib.lcpp_reduce_by_key(0, L.I32, L.I32, keys.data_ptr(), vals.data_ptr(),
+                                                       uk.data_ptr(), outv.data_ptr(), nr.data_ptr(), n,
+                                                       t.data_ptr(), tb, sh)), 20)
+    runs = int(nr.item())
+    byts = 8 * n + 8 * runs
+    out[f"reduce_by_key_sum_i32_2p{28 - shrink}"] = {"ms": ms, "GB/s": byts / ms / 1e6, "frac": byts / ms / 1e6 / peak,
+                                                     "runs": runs}
     return out
 
 
