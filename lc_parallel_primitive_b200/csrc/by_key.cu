@@ -28,13 +28,15 @@
 //    16-entry scan of warp totals; warp 0 resolves the tile prefix by a
 //    warp-wide look-back (32 predecessors per poll, ordered reduction because
 //    the pair operator does not commute).
-//  * Descriptors: a status word per tile plus separate partial and inclusive
-//    pair slots; a slot is written before its status with release semantics
-//    and read after an acquire load of the status, so pairs of any width
-//    travel safely.  Every wait is bounded by g_spin_limit.
+//  * Descriptors: for 4-byte values and n < 2^30 one 64-bit word per tile
+//    {status | count | value} with relaxed accesses (no fences); otherwise a
+//    status word per tile plus separate partial and inclusive pair slots, a
+//    slot written before its status with release semantics and read after an
+//    acquire load of the status.  Every wait is bounded by g_spin_limit.
 //  * Outputs are staged in shared memory and written coalesced: the scanned
 //    values back through the same swizzle, the runs of ReduceByKey compacted
 //    to a dense range per tile.
+#include "bulk.cuh"
 #include "common.cuh"
 
 namespace lcpp {
@@ -100,19 +102,69 @@ __device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Two descriptor forms.  Packed (4-byte values, n < 2^30): one 64-bit word
+// per tile {status:2 | count:30 | value:32} written and read with relaxed
+// device-scope accesses, so no fence is needed.  Otherwise: a status word per
+// tile plus separate partial / inclusive pair slots, slot before status with
+// release / acquire ordering.
 template <typename T>
 struct BkDesc {
+    uint64_t* packed;     // non-null: packed form
     uint32_t* status;     // 0 = not ready, 1 = partial, 2 = inclusive
     KPair<T>* partial;
     KPair<T>* inclusive;
 };
 
 template <typename T>
+__device__ __forceinline__ uint64_t bk_pack(uint32_t st, const KPair<T>& p) {
+    uint32_t b;
+    memcpy(&b, &p.value, 4);
+    return (uint64_t)st << 62 | (uint64_t)(p.count & 0x3fffffffu) << 32 | b;
+}
+template <typename T>
+__device__ __forceinline__ KPair<T> bk_unpack(uint64_t w) {
+    KPair<T> p;
+    p.count = (uint32_t)(w >> 32) & 0x3fffffffu;
+    const uint32_t b = (uint32_t)w;
+    memcpy(&p.value, &b, 4);
+    return p;
+}
+
+template <typename T>
 __device__ __forceinline__ void bk_publish(const BkDesc<T>& d, int64_t tile, uint32_t st, const KPair<T>& p) {
+    if constexpr (sizeof(T) == 4) {
+        if (d.packed) {
+            st_relaxed_u64(d.packed + tile, bk_pack(st, p));
+            return;
+        }
+    }
     KPair<T>* slot = (st == 2 ? d.inclusive : d.partial) + tile;
     __stcg(&slot->count, p.count);
     __stcg(&slot->value, p.value);
     st_release_u32(d.status + tile, st);
+}
+
+// Status of tile p (0 = not ready), and its pair once ready.
+template <typename T>
+__device__ __forceinline__ uint32_t bk_poll(const BkDesc<T>& d, int64_t p, uint64_t& word) {
+    if constexpr (sizeof(T) == 4) {
+        if (d.packed) {
+            word = ld_relaxed_u64(d.packed + p);
+            return (uint32_t)(word >> 62);
+        }
+    }
+    return ld_acquire_u32(d.status + p);
+}
+template <typename T>
+__device__ __forceinline__ KPair<T> bk_fetch(const BkDesc<T>& d, int64_t p, uint32_t st, uint64_t word) {
+    if constexpr (sizeof(T) == 4) {
+        if (d.packed) return bk_unpack<T>(word);
+    }
+    KPair<T> v;
+    const KPair<T>* slot = (st == 2 ? d.inclusive : d.partial) + p;
+    v.count = __ldcg(&slot->count);
+    v.value = __ldcg(&slot->value);
+    return v;
 }
 
 // Warp-wide ordered look-back: the combination of the aggregates of tiles
@@ -126,21 +178,18 @@ __device__ KPair<T> bk_lookback(const BkDesc<T>& d, int64_t tile) {
     int64_t p = tile - 1 - lane;
     uint32_t spins = 0;
     while (true) {
-        uint32_t st = p >= 0 ? ld_acquire_u32(d.status + p) : 2u;
+        uint64_t word = 0;
+        uint32_t st = p >= 0 ? bk_poll(d, p, word) : 2u;
         while (__any_sync(0xffffffffu, st == 0)) {
             if (++spins > limit) {
                 if (lane == 0) set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
                 return acc;
             }
             if (spins > 64) __nanosleep(spins < 1024 ? 32 : 128);
-            if (st == 0) st = ld_acquire_u32(d.status + p);
+            if (st == 0) st = bk_poll(d, p, word);
         }
         KPair<T> v = kidentity<Op, T>();
-        if (p >= 0) {
-            const KPair<T>* slot = (st == 2 ? d.inclusive : d.partial) + p;
-            v.count = __ldcg(&slot->count);
-            v.value = __ldcg(&slot->value);
-        }
+        if (p >= 0) v = bk_fetch(d, p, st, word);
         const uint32_t incl = __ballot_sync(0xffffffffu, st == 2);
         const int first = incl ? __ffs(incl) - 1 : 32;
         if (lane > first) v = kidentity<Op, T>();
@@ -366,6 +415,281 @@ by_key_kernel(const K* __restrict__ keys, const T* values, T* out_values, K* __r
     }
 }
 
+// ---------------------------------------------------------------------------
+// Pipelined persistent form (16-byte-aligned keys, values and outputs).
+//
+// Persistent CTAs (2 per SM, 512 threads) stream tiles through three
+// shared-memory stages filled by TMA bulk copies (cp.async.bulk, this GPU's
+// memory only, no multicast).  A stage holds the tile's keys, its values and
+// the 16 bytes of keys just before the tile (the predecessor key), all landed
+// on one mbarrier.  As in the pipelined plain scan, a CTA publishes the
+// aggregate of its NEXT tile as soon as that tile lands, before it resolves
+// the look-back of its current tile, so partial descriptors run one tile
+// ahead of the scan frontier.  Per-thread state of a tile (head-flag mask and
+// the thread's exclusive pair within its warp) stays in registers between the
+// two phases; per-warp prefixes of each stage stay in shared memory.
+// Each thread owns 32 bytes of the wider of key and value: 8 items for
+// 4-byte keys and values, 4 items otherwise (tiles of 4096 / 2048 items).
+// ---------------------------------------------------------------------------
+constexpr int BKP_STAGES = 3;
+constexpr int BKP_CTAS_PER_SM = 2;
+constexpr int BK_DESC_TILE = 2048;  // smallest tile of any by-key kernel: sizes the descriptors
+
+template <typename K, typename T>
+struct BkpShape {
+    static constexpr int W = sizeof(K) > sizeof(T) ? sizeof(K) : sizeof(T);
+    static constexpr int ITEMS = 32 / W;
+    static constexpr int TILE = BK_THREADS * ITEMS;
+    static constexpr int KBYTES = TILE * sizeof(K);
+    static constexpr int VBYTES = TILE * sizeof(T);
+    static constexpr int STAGE = KBYTES + VBYTES + 16;  // + predecessor keys
+    static constexpr int KCH = ITEMS * sizeof(K) / 16;  // 16-byte chunks per thread
+    static constexpr int VCH = ITEMS * sizeof(T) / 16;
+    static_assert(TILE >= BK_DESC_TILE, "descriptor array sized for BK_DESC_TILE");
+};
+
+template <typename K, typename T, typename Op, int MODE>
+__global__ void __launch_bounds__(BK_THREADS, BKP_CTAS_PER_SM)
+by_key_pipe_kernel(const K* keys, const T* values, T* out_values, K* __restrict__ unique_out,
+                   uint32_t* __restrict__ num_runs_out, uint64_t n, uint64_t num_tiles, T init,
+                   unsigned int* ticket, BkDesc<T> desc) {
+    using S = BkpShape<K, T>;
+    constexpr int ITEMS = S::ITEMS, TILE = S::TILE;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t s_bar[BKP_STAGES];
+    __shared__ unsigned int s_tile[BKP_STAGES];
+    __shared__ KPair<T> s_wagg[BK_WARPS];
+    __shared__ KPair<T> s_wpre[BKP_STAGES][BK_WARPS];
+    __shared__ KPair<T> s_tagg[BKP_STAGES];
+    __shared__ KPair<T> s_tpre;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint64_t full_tiles = n / TILE;
+    const uint32_t limit = g_spin_limit;
+    uint32_t phase[BKP_STAGES] = {};
+
+    auto stage_keys = [&](int st) { return reinterpret_cast<K*>(smem + st * S::STAGE); };
+    auto stage_vals = [&](int st) { return reinterpret_cast<T*>(smem + st * S::STAGE + S::KBYTES); };
+    auto stage_pred = [&](int st) { return reinterpret_cast<K*>(smem + st * S::STAGE + S::KBYTES + S::VBYTES); };
+
+    auto issue = [&](unsigned int t, int st) {  // thread 0
+        if (t < full_tiles) {
+            fence_proxy_async_smem();
+            const uint64_t base = (uint64_t)t * TILE;
+            mbar_arrive_expect_tx(&s_bar[st], S::KBYTES + S::VBYTES + (t ? 16 : 0));
+            bulk_load(stage_keys(st), keys + base, S::KBYTES, &s_bar[st]);
+            bulk_load(stage_vals(st), values + base, S::VBYTES, &s_bar[st]);
+            if (t) bulk_load(stage_pred(st), reinterpret_cast<const char*>(keys + base) - 16, 16, &s_bar[st]);
+        }
+    };
+
+    // Blocked items of thread tid in stage st.
+    auto read_items = [&](int st, K (&k)[ITEMS], T (&v)[ITEMS]) {
+#pragma unroll
+        for (int c = 0; c < S::KCH; ++c) {
+            const uint4 q = reinterpret_cast<const uint4*>(stage_keys(st))[tid * S::KCH + c];
+            memcpy(&k[c * (16 / sizeof(K))], &q, 16);
+        }
+#pragma unroll
+        for (int c = 0; c < S::VCH; ++c) {
+            const uint4 q = reinterpret_cast<const uint4*>(stage_vals(st))[tid * S::VCH + c];
+            memcpy(&v[c * (16 / sizeof(T))], &q, 16);
+        }
+    };
+    auto prev_key = [&](int st) -> K {
+        return tid ? stage_keys(st)[tid * ITEMS - 1] : stage_pred(st)[16 / sizeof(K) - 1];
+    };
+
+    // Phase 1 of tile t in stage st: wait for its data, head flags, pair
+    // scans, publish the tile aggregate.  Returns the thread's flag mask and
+    // its exclusive pair within the warp.
+    auto aggregate = [&](uint64_t t, int st, uint32_t& flags, KPair<T>& wex) {
+        const uint64_t base = t * TILE;
+        if (t < full_tiles) {
+            if (!mbar_wait(&s_bar[st], phase[st], limit)) set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
+            phase[st] ^= 1;
+        } else {  // ragged last tile: guarded copy
+            K* sk = stage_keys(st);
+            T* sv = stage_vals(st);
+            for (int i = tid; i < TILE; i += BK_THREADS) {
+                const uint64_t g = base + i;
+                if (g < n) {
+                    sk[i] = keys[g];
+                    sv[i] = values[g];
+                }
+            }
+            if (tid == 0 && t > 0) stage_pred(st)[16 / sizeof(K) - 1] = keys[base - 1];
+            __syncthreads();
+        }
+        K k[ITEMS];
+        T v[ITEMS];
+        read_items(st, k, v);
+        const K kp0 = prev_key(st);
+        flags = 0;
+        KPair<T> agg = kidentity<Op, T>();
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const uint64_t i = base + (uint64_t)tid * ITEMS + j;
+            const K kp = j ? k[j - 1] : kp0;
+            bool head;
+            if (MODE == BK_REDUCE) head = i > 0 && i < n && key_differs(k[j], kp);
+            else head = i < n && (i == 0 || key_differs(k[j], kp));
+            flags |= (uint32_t)head << j;
+            KPair<T> it;
+            it.count = head;
+            it.value = i < n ? v[j] : Op::template identity<T>();
+            agg = kcombine<Op, T>(agg, it);
+        }
+        KPair<T> incl = agg;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const KPair<T> y = kshfl_up(incl, o);
+            if (lane >= o) incl = kcombine<Op, T>(y, incl);
+        }
+        wex = kshfl_up(incl, 1);
+        if (lane == 0) wex = kidentity<Op, T>();
+        __syncthreads();  // earlier readers of s_wagg are done
+        if (lane == 31) s_wagg[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            KPair<T> w = lane < BK_WARPS ? s_wagg[lane] : kidentity<Op, T>();
+#pragma unroll
+            for (int o = 1; o < BK_WARPS; o <<= 1) {
+                const KPair<T> y = kshfl_up(w, o);
+                if (lane >= o) w = kcombine<Op, T>(y, w);
+            }
+            KPair<T> wx = kshfl_up(w, 1);
+            if (lane == 0) wx = kidentity<Op, T>();
+            if (lane < BK_WARPS) s_wpre[st][lane] = wx;
+            if (lane == BK_WARPS - 1) {
+                s_tagg[st] = w;
+                bk_publish(desc, (int64_t)t, t == 0 ? 2u : 1u, w);
+            }
+        }
+    };
+
+    // Phase 2 of tile t: look-back, outputs.
+    auto scan_tile = [&](uint64_t t, int st, uint32_t flags, const KPair<T>& wex) {
+        const uint64_t base = t * TILE;
+        const bool full = t < full_tiles;
+        __syncthreads();  // s_wpre / s_tagg of this stage visible; s_tpre free
+        if (warp == 0) {
+            KPair<T> tpre = kidentity<Op, T>();
+            if (t != 0) {
+                tpre = bk_lookback<Op, T>(desc, (int64_t)t);
+                if (lane == 0) bk_publish(desc, (int64_t)t, 2u, kcombine<Op, T>(tpre, s_tagg[st]));
+            }
+            if (lane == 0) s_tpre = tpre;
+        }
+        __syncthreads();
+        const KPair<T> tpre = s_tpre;
+        KPair<T> run = kcombine<Op, T>(kcombine<Op, T>(tpre, s_wpre[st][warp]), wex);
+        K k[ITEMS];
+        T v[ITEMS];
+        read_items(st, k, v);
+        if (MODE != BK_REDUCE) {
+            T o[ITEMS];
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j) {
+                const bool head = (flags >> j) & 1u;
+                if (MODE == BK_SCAN_EXCL) {
+                    o[j] = head ? init : Op::template apply<T>(run.value, init);
+                    run.value = head ? v[j] : Op::template apply<T>(run.value, v[j]);
+                } else {
+                    run.value = head ? v[j] : Op::template apply<T>(run.value, v[j]);
+                    o[j] = Op::template apply<T>(run.value, init);
+                }
+            }
+            if (full) {
+#pragma unroll
+                for (int c = 0; c < S::VCH; ++c) {
+                    uint4 q;
+                    memcpy(&q, &o[c * (16 / sizeof(T))], 16);
+                    reinterpret_cast<uint4*>(stage_vals(st))[tid * S::VCH + c] = q;
+                }
+                fence_proxy_async_smem();
+                __syncthreads();
+                if (tid == 0) {
+                    bulk_store(out_values + base, stage_vals(st), S::VBYTES);
+                    bulk_commit();
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < ITEMS; ++j) {
+                    const uint64_t i = base + (uint64_t)tid * ITEMS + j;
+                    if (i < n) out_values[i] = o[j];
+                }
+            }
+        } else {
+            const K kp0 = prev_key(st);
+            const uint32_t c0 = tpre.count;
+            const uint32_t ntile = s_tagg[st].count;
+            __syncthreads();  // every thread holds its items: the stage is free for compaction
+            K* s_uk = stage_keys(st);
+            T* s_agg = stage_vals(st);
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j) {
+                const bool head = (flags >> j) & 1u;
+                if (head) {
+                    const uint32_t pos = run.count - c0;
+                    s_uk[pos] = j ? k[j - 1] : kp0;
+                    s_agg[pos] = run.value;
+                }
+                run.count += head;
+                run.value = head ? v[j] : Op::template apply<T>(run.value, v[j]);
+                if (base + (uint64_t)tid * ITEMS + j == n - 1) {  // the run that ends the input
+                    unique_out[run.count] = k[j];
+                    out_values[run.count] = run.value;
+                    *num_runs_out = run.count + 1;
+                }
+            }
+            __syncthreads();
+            for (uint32_t e = tid; e < ntile; e += BK_THREADS) {
+                unique_out[c0 + e] = s_uk[e];
+                out_values[c0 + e] = s_agg[e];
+            }
+        }
+    };
+
+    if (tid == 0) {
+        for (int i = 0; i < BKP_STAGES; ++i) mbar_init(&s_bar[i], 1);
+        fence_mbar_init();
+        for (int i = 0; i < BKP_STAGES; ++i) {
+            const unsigned int t = atomicAdd(ticket, 1u);
+            s_tile[i] = t;
+            issue(t, i);
+        }
+    }
+    __syncthreads();
+
+    uint64_t c = s_tile[0];
+    int st = 0;
+    uint32_t fl_c = 0, fl_n = 0;
+    KPair<T> wx_c = kidentity<Op, T>(), wx_n = kidentity<Op, T>();
+    if (c < num_tiles) aggregate(c, 0, fl_c, wx_c);
+    while (c < num_tiles) {
+        const int nst = st + 1 == BKP_STAGES ? 0 : st + 1;
+        const uint64_t nt = s_tile[nst];
+        // The ticket for the stage this iteration frees is taken now by warp
+        // 1, so the atomic's round trip overlaps the two phases below.
+        const unsigned int pref = tid == 32 ? atomicAdd(ticket, 1u) : 0u;
+        if (nt < num_tiles) aggregate(nt, nst, fl_n, wx_n);
+        scan_tile(c, st, fl_c, wx_c);
+        if (tid == 32) s_tile[st] = pref;
+        __syncthreads();
+        if (tid == 0) {
+            bulk_wait_read_all();  // this stage's bulk store has read it
+            issue(s_tile[st], st);
+        }
+        __syncthreads();
+        c = nt;
+        st = nst;
+        fl_c = fl_n;
+        wx_c = wx_n;
+    }
+    if (tid == 0) bulk_wait_all();
+}
+
 template <typename K, typename T>
 constexpr int bk_items() { return (sizeof(K) == 4 && sizeof(T) == 4) ? 16 : 8; }
 
@@ -374,21 +698,37 @@ static lcpp_status bk_launch(const void* keys, const void* values, void* out_val
                              uint32_t* num_runs, uint64_t n, T init, void* temp, cudaStream_t s) {
     constexpr int ITEMS = bk_items<K, T>();
     constexpr int TILE = BK_THREADS * ITEMS;
-    const uint64_t tiles = ceil_div(n, TILE);
+    const uint64_t tiles = ceil_div(n, BK_DESC_TILE);  // descriptor slots (>= tiles of either kernel)
     unsigned int* ticket = (unsigned int*)temp;
     BkDesc<T> d;
+    const bool packed = sizeof(T) == 4 && n < (1ull << 30);
     d.status = (uint32_t*)((char*)temp + BK_HDR);
-    d.partial = (KPair<T>*)((char*)d.status + align_up(tiles * 4, 256));
+    d.packed = packed ? (uint64_t*)d.status : nullptr;
+    d.partial = (KPair<T>*)((char*)d.status + align_up(tiles * 8, 256));
     d.inclusive = (KPair<T>*)((char*)d.partial + align_up(tiles * sizeof(KPair<T>), 256));
-    if (cudaMemsetAsync(temp, 0, BK_HDR + tiles * 4, s) != cudaSuccess) return LCPP_ERR_CUDA;
+    if (cudaMemsetAsync(temp, 0, BK_HDR + tiles * (packed ? 8 : 4), s) != cudaSuccess) return LCPP_ERR_CUDA;
     const bool vec = ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values) |
                        (MODE == BK_REDUCE ? 0 : reinterpret_cast<uintptr_t>(out_values))) & 15) == 0;
+    ProfScope ps(MODE == BK_REDUCE ? "reduce_by_key" : "scan_by_key", s);
+    if (vec) {
+        using SP = BkpShape<K, T>;
+        const uint64_t ptiles = ceil_div(n, SP::TILE);
+        const size_t psmem = (size_t)BKP_STAGES * SP::STAGE;
+        uint64_t grid = (uint64_t)device_info().sms * BKP_CTAS_PER_SM;
+        if (grid > ceil_div(ptiles, 2)) grid = ceil_div(ptiles, 2);
+        auto pk = by_key_pipe_kernel<K, T, Op, MODE>;
+        if (cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) != cudaSuccess)
+            return LCPP_ERR_CUDA;
+        pk<<<(unsigned)grid, BK_THREADS, psmem, s>>>((const K*)keys, (const T*)values, (T*)out_values,
+                                                      (K*)unique_out, num_runs, n, ptiles, init, ticket, d);
+        count_launch();
+        return check_launch();
+    }
     const size_t smem = (size_t)TILE * (sizeof(K) + sizeof(T));
     auto kern = by_key_kernel<K, T, Op, MODE, ITEMS>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return LCPP_ERR_CUDA;
-    ProfScope ps(MODE == BK_REDUCE ? "reduce_by_key" : "scan_by_key", s);
-    kern<<<(unsigned)tiles, BK_THREADS, smem, s>>>((const K*)keys, (const T*)values, (T*)out_values,
+    kern<<<(unsigned)ceil_div(n, TILE), BK_THREADS, smem, s>>>((const K*)keys, (const T*)values, (T*)out_values,
                                                    (K*)unique_out, num_runs, n, init, vec, ticket, d);
     count_launch();
     return check_launch();
@@ -397,10 +737,9 @@ static lcpp_status bk_launch(const void* keys, const void* values, void* out_val
 static size_t bk_temp_bytes(int key_dtype, int value_dtype, uint64_t n) {
     const size_t ks = lcpp_dtype_size(key_dtype), vs = lcpp_dtype_size(value_dtype);
     if (!ks || !vs) return 0;
-    const uint64_t items = BK_THREADS * ((ks == 4 && vs == 4) ? 16 : 8);
-    const uint64_t tiles = ceil_div(n ? n : 1, items);
+    const uint64_t tiles = ceil_div(n ? n : 1, BK_DESC_TILE);
     const size_t pair = vs == 8 ? 16 : 8;
-    return BK_HDR + align_up(tiles * 4, 256) + 2 * align_up(tiles * pair, 256);
+    return BK_HDR + align_up(tiles * 8, 256) + 2 * align_up(tiles * pair, 256);
 }
 
 // Key dispatch: integer keys compare by bits, float keys by value.
