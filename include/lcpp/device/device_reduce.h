@@ -1,8 +1,8 @@
 /*
  * DeviceReduce — same class template, methods and argument meaning as the
  * reference (src/lcpp/device/device_reduce.h:41-325); the work runs in the
- * sm_100a kernels of liblcpp_b200.so through lcpp_reduce(), lcpp_arg_reduce()
- * and lcpp_reduce_by_key().
+ * sm_100a kernels of liblcpp_b200.so through lcpp_reduce(), lcpp_transform_reduce(),
+ * lcpp_arg_reduce() and lcpp_reduce_by_key().
  */
 #pragma once
 #include "lcpp/runtime/core.h"
@@ -61,6 +61,19 @@ class DeviceReduce : public LuisaModule {
     void ArgMax(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
                 BufferView<Type4Byte> d_out, BufferView<uint> d_index_out, size_t num_item) {
         record_arg(cmdlist, LCPP_OP_MAX, temp_storage, d_in, d_out, d_index_out, num_item);
+    }
+
+    // Reference: device_reduce.h:331-348.  ReduceOp: SumOp / MinOp / MaxOp;
+    // TransformOp: IdentityOp / SquareOp / AbsOp / NegateOp.  Temp: GetTempStorageBytes.
+    template <NumericT Type4Byte, typename ReduceOp, typename TransformOp>
+    void TransformReduce(CommandList& cmdlist, BufferView<uint> temp_storage, BufferView<Type4Byte> d_in,
+                         BufferView<Type4Byte> d_out, size_t num_item, ReduceOp, TransformOp, Type4Byte init) {
+        const int op = ReduceOp::lcpp_op, xf = TransformOp::lcpp_xf;
+        cmdlist << [=](cudaStream_t s) {
+            return lcpp_transform_reduce(op, xf, lcpp_dtype_of<Type4Byte>(), d_in.data(), d_out.data(), num_item,
+                                         &init, temp_storage.data(), temp_storage.size_bytes(), s);
+        };
+        lcpp_check(cmdlist, m_debug_stream);
     }
 
     // Reference: device_reduce.h:110-125 (temp size), 277-325.  ReduceOp must

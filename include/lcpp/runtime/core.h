@@ -229,6 +229,12 @@ constexpr int lcpp_dtype_of() {
 struct SumOp { static constexpr int lcpp_op = LCPP_OP_SUM; };
 struct MinOp { static constexpr int lcpp_op = LCPP_OP_MIN; };
 struct MaxOp { static constexpr int lcpp_op = LCPP_OP_MAX; };
+// Element transforms for DeviceReduce::TransformReduce (the reference's DSL
+// transform lambdas cannot cross the C ABI).
+struct IdentityOp { static constexpr int lcpp_xf = LCPP_XF_IDENTITY; };
+struct SquareOp { static constexpr int lcpp_xf = LCPP_XF_SQUARE; };
+struct AbsOp { static constexpr int lcpp_xf = LCPP_XF_ABS; };
+struct NegateOp { static constexpr int lcpp_xf = LCPP_XF_NEGATE; };
 
 template <typename T>
 concept NumericT = std::is_integral_v<T> || std::is_floating_point_v<T>;

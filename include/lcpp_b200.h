@@ -189,6 +189,17 @@ lcpp_status lcpp_segment_arg_reduce_fixed(int op, int dtype, const void* in, voi
                                           uint32_t* out_index, uint64_t num_segments,
                                           uint64_t segment_size, void* stream);
 
+/* ---- TransformReduce ----------------------------------------------------
+ * out = op(init, reduce_op over transform(in[i])).  Replaces DeviceReduce::
+ * TransformReduce (device_reduce.h:331-348), whose reduce and transform
+ * operators are DSL lambdas: here op is LCPP_OP_SUM/MIN/MAX and transform one
+ * of the LCPP_XF_* element maps below (integer square / negate wrap).  init is
+ * a HOST pointer to one element of dtype (NULL = the op's identity).  Temp:
+ * lcpp_reduce_temp_bytes. */
+enum { LCPP_XF_IDENTITY = 0, LCPP_XF_SQUARE = 1, LCPP_XF_ABS = 2, LCPP_XF_NEGATE = 3 };
+lcpp_status lcpp_transform_reduce(int op, int transform, int dtype, const void* in, void* out, uint64_t n,
+                                  const void* init, void* temp, size_t temp_bytes, void* stream);
+
 /* ---- ScanByKey / ReduceByKey ------------------------------------------
  * Segments are runs of equal consecutive keys (a new one starts where
  * keys[i] != keys[i-1]; float keys compare by value).  op in {SUM, MIN, MAX};

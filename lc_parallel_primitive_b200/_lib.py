@@ -18,6 +18,7 @@ I32, U32, F32, I64, U64, F64, NONE = 0, 1, 2, 3, 4, 5, 15
 OP_SUM, OP_MIN, OP_MAX = 0, 1, 2
 # lcpp_scan_kind
 SCAN_EXCLUSIVE, SCAN_INCLUSIVE = 0, 1
+XF_IDENTITY, XF_SQUARE, XF_ABS, XF_NEGATE = 0, 1, 2, 3
 # lcpp_status
 OK = 0
 ERR_INVALID_ARG = -1
@@ -51,6 +52,7 @@ SIGNATURES = {
     "lcpp_arg_reduce": (_i, [_i, _i, _vp, _vp, _vp, _u64, _vp, _sz, _vp]),
     "lcpp_segment_arg_reduce": (_i, [_i, _i, _vp, _vp, _vp, _u64, _vp, _vp, _vp]),
     "lcpp_segment_arg_reduce_fixed": (_i, [_i, _i, _vp, _vp, _vp, _u64, _u64, _vp]),
+    "lcpp_transform_reduce": (_i, [_i, _i, _i, _vp, _vp, _u64, _vp, _vp, _sz, _vp]),
     "lcpp_scan_by_key_temp_bytes": (_sz, [_i, _i, _u64]),
     "lcpp_scan_by_key": (_i, [_i, _i, _i, _i, _vp, _vp, _vp, _u64, _vp, _vp, _sz, _vp]),
     "lcpp_reduce_by_key_temp_bytes": (_sz, [_i, _i, _u64]),

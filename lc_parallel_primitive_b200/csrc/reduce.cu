@@ -11,6 +11,7 @@
 // combined in-kernel by the last CTA to finish, in a fixed order, so float
 // results are deterministic for a given n and GPU.
 #include "common.cuh"
+#include <type_traits>
 
 namespace lcpp {
 
@@ -32,19 +33,56 @@ __device__ __forceinline__ T block_reduce(T v, T* s_warp) {
     return v;  // valid in warp 0
 }
 
+// Element transforms of TransformReduce (the reference takes a DSL lambda,
+// device_reduce.h:331-348; a C ABI carries one of these instead).  Integer
+// square and negate wrap modulo 2^bits.  Each takes the kernel's runtime
+// factor k (-1 for negate, unused otherwise): negation is a multiply by a
+// value the compiler cannot see, because on this toolchain a max reduction
+// over compiler-visible negations (0 - x, whatever its spelling) came out
+// with some elements not negated.
+struct XfIdentity { template <typename T> static __device__ __forceinline__ T apply(T x, T) { return x; } };
+struct XfSquare {
+    template <typename T> static __device__ __forceinline__ T apply(T x, T) {
+        if constexpr (std::is_floating_point<T>::value) return x * x;
+        else {
+            using U = typename Unsigned<T>::type;
+            return (T)((U)x * (U)x);
+        }
+    }
+};
+struct XfAbs {
+    template <typename T> static __device__ __forceinline__ T apply(T x, T) {
+        if constexpr (std::is_unsigned<T>::value) return x;
+        else if constexpr (std::is_floating_point<T>::value) return x < T(0) ? -x : x;  // -0 and NaN kept
+        else {
+            using U = typename Unsigned<T>::type;
+            return x < T(0) ? (T)(U(0) - (U)x) : x;
+        }
+    }
+};
+struct XfNegate {
+    template <typename T> static __device__ __forceinline__ T apply(T x, T k) {
+        if constexpr (std::is_floating_point<T>::value) return x * k;
+        else {
+            using U = typename Unsigned<T>::type;
+            return (T)((U)x * (U)k);
+        }
+    }
+};
+
 // Accumulate the 16-byte vector `q` (VEC elements of T) into acc.
-template <typename Op, typename T, int VEC>
-__device__ __forceinline__ T fold_vec(T acc, const uint4& q) {
+template <typename Op, typename T, int VEC, typename Xf = XfIdentity>
+__device__ __forceinline__ T fold_vec(T acc, const uint4& q, T k = T(0)) {
     const T* e = reinterpret_cast<const T*>(&q);
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) acc = Op::template apply<T>(acc, e[i]);
+    for (int i = 0; i < VEC; ++i) acc = Op::template apply<T>(acc, Xf::template apply<T>(e[i], k));
     return acc;
 }
 
-template <typename Op, typename T>
+template <typename Op, typename T, typename Xf = XfIdentity>
 __global__ void __launch_bounds__(REDUCE_THREADS)
 reduce_kernel(const T* __restrict__ in, uint64_t n, T* __restrict__ partials,
-              unsigned int* __restrict__ ticket, T* __restrict__ out, T init) {
+              unsigned int* __restrict__ ticket, T* __restrict__ out, T init, T k = T(0)) {
     constexpr int VEC = 16 / sizeof(T);
     __shared__ T s_warp[REDUCE_THREADS / 32];
     __shared__ bool s_last;
@@ -56,7 +94,7 @@ reduce_kernel(const T* __restrict__ in, uint64_t n, T* __restrict__ partials,
     if (head > n) head = n;
     const uint64_t gtid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t gstride = (uint64_t)gridDim.x * blockDim.x;
-    if (gtid < head) acc = Op::template apply<T>(acc, in[gtid]);
+    if (gtid < head) acc = Op::template apply<T>(acc, Xf::template apply<T>(in[gtid], k));
 
     const uint4* vin = reinterpret_cast<const uint4*>(in + head);
     const uint64_t nvec = (n - head) / VEC;
@@ -66,11 +104,11 @@ reduce_kernel(const T* __restrict__ in, uint64_t n, T* __restrict__ partials,
 #pragma unroll
         for (int u = 0; u < REDUCE_UNROLL; ++u) q[u] = ld_stream(vin + i + u * gstride);
 #pragma unroll
-        for (int u = 0; u < REDUCE_UNROLL; ++u) acc = fold_vec<Op, T, VEC>(acc, q[u]);
+        for (int u = 0; u < REDUCE_UNROLL; ++u) acc = fold_vec<Op, T, VEC, Xf>(acc, q[u], k);
     }
-    for (; i < nvec; i += gstride) acc = fold_vec<Op, T, VEC>(acc, ld_stream(vin + i));
+    for (; i < nvec; i += gstride) acc = fold_vec<Op, T, VEC, Xf>(acc, ld_stream(vin + i), k);
     const uint64_t tail0 = head + nvec * VEC;
-    if (tail0 + gtid < n) acc = Op::template apply<T>(acc, in[tail0 + gtid]);
+    if (tail0 + gtid < n) acc = Op::template apply<T>(acc, Xf::template apply<T>(in[tail0 + gtid], k));
 
     acc = block_reduce<Op>(acc, s_warp);
     if (!ticket) {  // two-kernel form: reduce_final_kernel combines the partials
@@ -110,9 +148,10 @@ reduce_final_kernel(const T* __restrict__ partials, unsigned int count, T* __res
     if (threadIdx.x == 0) out[0] = Op::template apply<T>(init, v);
 }
 
-template <typename Op, typename T>
-static lcpp_status reduce_two_kernels(const T* in, uint64_t n, T* part, T* out, unsigned grid, cudaStream_t s) {
-    reduce_kernel<Op, T><<<grid, REDUCE_THREADS, 0, s>>>(in, n, part, nullptr, out, Op::template identity<T>());
+template <typename Op, typename T, typename Xf = XfIdentity>
+static lcpp_status reduce_two_kernels(const T* in, uint64_t n, T* part, T* out, unsigned grid, cudaStream_t s,
+                                      T init = Op::template identity<T>(), T k = T(0)) {
+    reduce_kernel<Op, T, Xf><<<grid, REDUCE_THREADS, 0, s>>>(in, n, part, nullptr, out, Op::template identity<T>(), k);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(REDUCE_THREADS);
@@ -122,8 +161,7 @@ static lcpp_status reduce_two_kernels(const T* in, uint64_t n, T* part, T* out, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, reduce_final_kernel<Op, T>, (const T*)part, grid, out, Op::template identity<T>()) !=
-        cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, reduce_final_kernel<Op, T>, (const T*)part, grid, out, init) != cudaSuccess)
         return LCPP_ERR_CUDA;
     count_launch(2);
     return check_launch();
@@ -197,5 +235,38 @@ extern "C" lcpp_status lcpp_reduce(int op, int dtype, const void* in, void* out,
         }
         count_launch();
         return check_launch();
+    });
+}
+
+extern "C" lcpp_status lcpp_transform_reduce(int op, int transform, int dtype, const void* in, void* out,
+                                             uint64_t n, const void* init, void* temp, size_t temp_bytes,
+                                             void* stream) {
+    if (!out || (!in && n) || op < 0 || op > 2 || transform < 0 || transform > 3) return LCPP_ERR_INVALID_ARG;
+    const size_t need = lcpp_reduce_temp_bytes(dtype, n);
+    if (!need) return LCPP_ERR_INVALID_ARG;
+    if (!temp || temp_bytes < need) return LCPP_ERR_TEMP_TOO_SMALL;
+    cudaStream_t s = (cudaStream_t)stream;
+    return dispatch_dtype(dtype, [&](auto zero) -> lcpp_status {
+        using T = decltype(zero);
+        const unsigned int grid = reduce_grid(n, sizeof(T));
+        const T* pin = (const T*)in;
+        T* pout = (T*)out;
+        T* part = (T*)((char*)temp + 256);
+        ProfScope ps("reduce", s);
+        auto go = [&](auto opv) -> lcpp_status {
+            using Op = decltype(opv);
+            const T iv = init ? *(const T*)init : Op::template identity<T>();
+            switch (transform) {
+                case LCPP_XF_IDENTITY: return reduce_two_kernels<Op, T, XfIdentity>(pin, n, part, pout, grid, s, iv);
+                case LCPP_XF_SQUARE: return reduce_two_kernels<Op, T, XfSquare>(pin, n, part, pout, grid, s, iv);
+                case LCPP_XF_ABS: return reduce_two_kernels<Op, T, XfAbs>(pin, n, part, pout, grid, s, iv);
+                default: return reduce_two_kernels<Op, T, XfNegate>(pin, n, part, pout, grid, s, iv, (T)-1);
+            }
+        };
+        switch (op) {
+            case LCPP_OP_SUM: return go(OpSum{});
+            case LCPP_OP_MIN: return go(OpMin{});
+            default: return go(OpMax{});
+        }
     });
 }

@@ -185,6 +185,22 @@ class DeviceReduce(_Module):
     def Max(self, cmdlist, temp_storage, d_in, d_out, num_item):
         self.Reduce(cmdlist, temp_storage, d_in, d_out, num_item, L.OP_MAX)
 
+    def TransformReduce(self, cmdlist, temp_storage, d_in, d_out, num_item, reduce_op, transform_op, init):
+        """reduce_op: "sum" | "min" | "max"; transform_op: "identity" | "square" | "abs" | "negate"
+        (the reference's DSL lambdas, device_reduce.h:331-348); out = reduce_op(init, reduce(transform(x)))."""
+        dt = lcpp_dtype(d_in)
+        if lcpp_dtype(d_out) != dt:
+            raise TypeError("d_in and d_out must have the same element type")
+        op = _op_code(reduce_op)
+        xf = {"identity": L.XF_IDENTITY, "square": L.XF_SQUARE, "abs": L.XF_ABS,
+              "negate": L.XF_NEGATE}[transform_op] if isinstance(transform_op, str) else int(transform_op)
+        iv = _host_scalar(init, dt)
+        pin, pout, ptmp, nt = _ptr(d_in), _ptr(d_out), _ptr(temp_storage), _nbytes(temp_storage)
+        self._record(cmdlist,
+                     lambda s: L.lib().lcpp_transform_reduce(op, xf, dt, pin, pout, num_item, iv.ctypes.data, ptmp,
+                                                             nt, s),
+                     "DeviceReduce.TransformReduce")
+
     @staticmethod
     def GetArgTempStorageBytes(num_item: int, dtype=torch.int32) -> int:
         return int(L.lib().lcpp_arg_reduce_temp_bytes(lcpp_dtype(dtype), num_item))

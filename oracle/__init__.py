@@ -44,11 +44,12 @@ def lib():
         h.oracle_scan_mt.argtypes = [i, i, vp, vp, u64, i]
         h.oracle_segment_reduce_mt.argtypes = [i, i, vp, vp, u64, vp, vp, i]
         h.oracle_scan_by_key.argtypes = [i, i, i, i, vp, vp, u64, vp, vp]
+        h.oracle_transform_reduce.argtypes = [i, i, i, vp, u64, vp, vp]
         h.oracle_reduce_by_key.argtypes = [i, i, i, vp, vp, u64, vp, vp, vp]
         for f in ("oracle_reduce", "oracle_scan", "oracle_abs_prefix_f32", "oracle_radix_sort",
                   "oracle_segment_reduce", "oracle_reduce_sum_mt", "oracle_scan_mt",
                   "oracle_segment_reduce_mt", "oracle_arg_reduce", "oracle_segment_arg_reduce", "oracle_scan_op",
-                  "oracle_scan_by_key", "oracle_reduce_by_key"):
+                  "oracle_scan_by_key", "oracle_reduce_by_key", "oracle_transform_reduce"):
             getattr(h, f).restype = i
         _lib = h
     return _lib
@@ -203,3 +204,15 @@ def reduce_by_key(op: int, keys: np.ndarray, values: np.ndarray):
                                    _p(agg), _p(nr)), "reduce_by_key")
     r = int(nr[0])
     return uk[:r], agg[:r], r
+
+
+def transform_reduce(op: int, xf: int, x: np.ndarray, init=None):
+    """op(init, reduce(xf(x))); xf 0 identity, 1 square, 2 abs, 3 negate.
+    Integer: exact wrapped value in x.dtype.  Float: fp64 value."""
+    x = np.ascontiguousarray(x)
+    if init is None:
+        init = {OP_SUM: 0, OP_MIN: _limits(x.dtype)[1], OP_MAX: _limits(x.dtype)[0]}[op]
+    iv = np.array([init], dtype=x.dtype)
+    out = np.zeros(1, dtype=np.float64 if x.dtype.kind == "f" else x.dtype)
+    _ok(lib().oracle_transform_reduce(op, xf, _dt(x), _p(x), x.size, _p(iv), _p(out)), "transform_reduce")
+    return out[0]

@@ -267,6 +267,26 @@ int main(int argc, char* argv[]) {
         }
     }
 
+    // ---- device_reduce_test.cpp:92-116 (TransformReduce: max of squares) ----------
+    {
+        const int N = 1 << 12;
+        std::vector<int32> input(N);
+        std::iota(input.begin(), input.end(), 0);
+        std::mt19937 rng(114521);
+        std::shuffle(input.begin(), input.end(), rng);
+        DeviceReduce<> reducer;
+        reducer.create(device, &stream);
+        auto in = device.create_buffer<int32>(N);
+        auto out = device.create_buffer<int32>(1);
+        stream << in.copy_from(input.data()) << synchronize();
+        auto temp = device.create_buffer<uint>(bytes_to_uint_count(DeviceReduce<>::GetTempStorageBytes<int32>(N)));
+        CommandList cmdlist;
+        reducer.TransformReduce(cmdlist, temp.view(), in.view(), out.view(), in.size(), MaxOp{}, SquareOp{}, 0);
+        std::vector<int32> r(1);
+        stream << cmdlist.commit() << synchronize() << out.copy_to(r.data()) << synchronize();
+        EXPECT(r[0] == (N - 1) * (N - 1), "transform reduce %d", r[0]);
+    }
+
     // ---- device_scan_test.cpp:111-167 (ExclusiveSumByKey) / device_reduce_test.cpp:229-295 --
     {
         DeviceScan<> scanner;
