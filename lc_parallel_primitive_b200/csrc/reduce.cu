@@ -16,9 +16,9 @@
 namespace lcpp {
 
 constexpr int REDUCE_THREADS = 512;
-constexpr int REDUCE_CTAS_PER_SM = 4;
+constexpr int REDUCE_CTAS_PER_SM = 8;
 constexpr int REDUCE_UNROLL = 4;   // independent 16-byte loads in flight per thread
-constexpr int REDUCE_MAX_GRID = 148 * 8;
+constexpr int REDUCE_MAX_GRID = 148 * 16;
 
 template <typename Op, typename T>
 __device__ __forceinline__ T block_reduce(T v, T* s_warp) {
