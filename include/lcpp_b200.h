@@ -44,7 +44,8 @@ enum {
     LCPP_ERR_CUDA             = -3, /* a CUDA runtime call or launch failed      */
     LCPP_ERR_LOOKBACK_TIMEOUT = -4, /* a look-back wait hit its iteration cap    */
     LCPP_ERR_NCCL             = -5, /* an NCCL call failed (multi-GPU entries)   */
-    LCPP_ERR_UNSUPPORTED      = -6  /* valid request this build does not serve   */
+    LCPP_ERR_UNSUPPORTED      = -6, /* valid request this build does not serve   */
+    LCPP_ERR_CAPACITY         = -7  /* multi-GPU sort: rank's slice > capacity   */
 };
 
 /* Element types.  The reference's NumericT (common/type_trait.h:11-14) admits
@@ -228,6 +229,61 @@ lcpp_status lcpp_reduce_by_key(int op, int key_dtype, int value_dtype, const voi
                                uint32_t* num_runs_out, uint64_t n, void* temp, size_t temp_bytes,
                                void* stream);
 
+
+/* ---- Multi-GPU (one process per GPU, NCCL) -----------------------------
+ * No counterpart in the reference, which is single-GPU and limits item
+ * counts to 32 bits (device_radix_sort.h:136, details/scan.h:72).  These
+ * extend DeviceReduce::Sum/Min/Max (device_reduce.h:169-185),
+ * DeviceScan::ExclusiveSum/InclusiveSum (device_scan.h:180-204) and
+ * DeviceRadixSort::SortPairs/SortKeys (device_radix_sort.h:129-153) to data
+ * sharded over the ranks of an NCCL communicator: the global sequence is
+ * the concatenation of the ranks' shards in rank order.  `comm` is an
+ * ncclComm_t passed as void*; every rank of it must make the same call.
+ * NCCL is loaded at run time (libnccl.so.2); without it these return
+ * LCPP_ERR_NCCL.  Scratch comes from `temp`; nothing is allocated. */
+size_t      lcpp_mg_unique_id_bytes(void);                 /* sizeof(ncclUniqueId) */
+lcpp_status lcpp_mg_get_unique_id(void* id_out);           /* ncclGetUniqueId */
+lcpp_status lcpp_mg_comm_init_rank(void** comm_out, int nranks, const void* id, int rank);
+lcpp_status lcpp_mg_comm_destroy(void* comm);
+lcpp_status lcpp_mg_comm_shape(void* comm, int* rank, int* nranks);
+
+/* *out (device, every rank) = op over all ranks' shards.  Asynchronous. */
+size_t      lcpp_mg_reduce_temp_bytes(int dtype, uint64_t n_local);
+lcpp_status lcpp_mg_reduce(int op, int dtype, const void* in, void* out, uint64_t n_local,
+                           void* temp, size_t temp_bytes, void* comm, void* stream);
+
+/* Prefix sum of the global sequence; each rank writes its shard's part.
+ * Local reduce -> all-gather of the G shard totals -> carry = sum of the
+ * lower ranks' totals (rank order) -> local scan seeded with the carry.
+ * Integer results are bit-exact (mod 2^bits).  dtype: I32 U32 F32.
+ * Asynchronous. */
+size_t      lcpp_mg_scan_temp_bytes(int dtype, uint64_t n_local, int nranks);
+lcpp_status lcpp_mg_scan(int kind, int dtype, const void* in, void* out, uint64_t n_local,
+                         void* temp, size_t temp_bytes, void* comm, void* stream);
+
+/* Global stable ascending sort of (key, value) pairs (value_dtype LCPP_NONE:
+ * keys only).  Rank r receives the r-th contiguous slice of the sorted global
+ * sequence in keys_out/values_out (room for `capacity` items, capacity >=
+ * n_local) and its length in *n_out (host).  Ranks are cut at splitters
+ * sampled from every shard (4096 samples per rank) on the extended key
+ * (key, rank, index), so slices are near n_total / nranks whatever the key
+ * distribution, duplicates included; a slice longer than capacity returns
+ * LCPP_ERR_CAPACITY.  At most 256 ranks.  Equal keys keep
+ * their global input order.  Waits once on `stream` (for the exchange
+ * sizes); the rest is asynchronous.  n_local, capacity < 2^32. */
+size_t      lcpp_mg_sort_temp_bytes(int key_dtype, int value_dtype, uint64_t n_local,
+                                    uint64_t capacity, int nranks);
+lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* keys_in, const void* values_in,
+                         uint64_t n_local, void* keys_out, void* values_out, uint64_t capacity,
+                         uint64_t* n_out, void* temp, size_t temp_bytes, void* comm, void* stream);
+/* The sort's splitter choice on the host (the device computes the same):
+ * given the gathered samples in ascending extended-key order (key image,
+ * position = rank << 32 | index) with their weights, splitter r-1 (r = 1 ..
+ * nranks-1) is the sample where the running weight crosses r/nranks of the
+ * total.  Host pointers; no GPU needed. */
+lcpp_status lcpp_mg_pick_splitters(const uint64_t* keys, const uint64_t* pos, const uint64_t* weights,
+                                   uint64_t count, int nranks, uint64_t* split_keys, uint64_t* split_pos);
+
 /* ---- Device error word --------------------------------------------------
  * Synchronizes `stream`, returns the first device-side error latched since
  * the last call on the current device (LCPP_OK if none) and clears it.  The
@@ -270,6 +326,10 @@ lcpp_status lcpp_profile_read(const char* kernel, uint64_t* launches, double* to
 /* Number of kernels this library launched from the calling process (all
  * devices, all streams) since load; for launch accounting in benchmarks. */
 uint64_t    lcpp_kernel_launch_count(void);
+/* Binary version (major*10+minor, e.g. 100 for sm_100a) of the library's
+ * kernels on the current device (cudaFuncGetAttributes), or a negative
+ * lcpp_status. */
+int         lcpp_kernel_binary_version(void);
 const char* lcpp_build_info(void);
 
 #ifdef __cplusplus

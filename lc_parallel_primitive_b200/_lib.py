@@ -27,6 +27,7 @@ ERR_CUDA = -3
 ERR_LOOKBACK_TIMEOUT = -4
 ERR_NCCL = -5
 ERR_UNSUPPORTED = -6
+ERR_CAPACITY = -7
 
 _vp, _u64, _sz, _i, _u32 = C.c_void_p, C.c_uint64, C.c_size_t, C.c_int, C.c_uint32
 
@@ -57,6 +58,19 @@ SIGNATURES = {
     "lcpp_scan_by_key": (_i, [_i, _i, _i, _i, _vp, _vp, _vp, _u64, _vp, _vp, _sz, _vp]),
     "lcpp_reduce_by_key_temp_bytes": (_sz, [_i, _i, _u64]),
     "lcpp_reduce_by_key": (_i, [_i, _i, _i, _vp, _vp, _vp, _vp, _vp, _u64, _vp, _sz, _vp]),
+    "lcpp_mg_unique_id_bytes": (_sz, []),
+    "lcpp_mg_get_unique_id": (_i, [_vp]),
+    "lcpp_mg_comm_init_rank": (_i, [C.POINTER(_vp), _i, _vp, _i]),
+    "lcpp_mg_comm_destroy": (_i, [_vp]),
+    "lcpp_mg_comm_shape": (_i, [_vp, C.POINTER(_i), C.POINTER(_i)]),
+    "lcpp_mg_reduce_temp_bytes": (_sz, [_i, _u64]),
+    "lcpp_mg_reduce": (_i, [_i, _i, _vp, _vp, _u64, _vp, _sz, _vp, _vp]),
+    "lcpp_mg_scan_temp_bytes": (_sz, [_i, _u64, _i]),
+    "lcpp_mg_scan": (_i, [_i, _i, _vp, _vp, _u64, _vp, _sz, _vp, _vp]),
+    "lcpp_mg_sort_temp_bytes": (_sz, [_i, _i, _u64, _u64, _i]),
+    "lcpp_mg_sort": (_i, [_i, _i, _vp, _vp, _u64, _vp, _vp, _u64, C.POINTER(_u64), _vp, _sz, _vp, _vp]),
+    "lcpp_mg_pick_splitters": (_i, [C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_u64), _u64, _i,
+                                    C.POINTER(_u64), C.POINTER(_u64)]),
     "lcpp_last_device_error": (_i, [_vp]),
     "lcpp_lookback_temp_bytes": (_sz, [_u64]),
     "lcpp_lookback_tiles": (_i, [_vp, _vp, _vp, _u64, _vp, _sz, _vp]),
@@ -65,6 +79,7 @@ SIGNATURES = {
     "lcpp_profile_enable": (_i, [_i]),
     "lcpp_profile_read": (_i, [C.c_char_p, C.POINTER(_u64), C.POINTER(C.c_double)]),
     "lcpp_kernel_launch_count": (_u64, []),
+    "lcpp_kernel_binary_version": (_i, []),
     "lcpp_build_info": (C.c_char_p, []),
 }
 
@@ -101,7 +116,7 @@ def _status_string(s: int) -> str:
         return lib().lcpp_status_string(s).decode()
     except Exception:  # library not loadable: still give a readable message
         return {0: "ok", -1: "invalid argument", -2: "temp storage too small", -3: "CUDA error",
-                -4: "look-back wait timed out", -5: "NCCL error", -6: "unsupported"}.get(s, "status")
+                -4: "look-back wait timed out", -5: "NCCL error", -6: "unsupported", -7: "output capacity exceeded"}.get(s, "status")
 
 
 def check(status: int, what: str = "") -> None:

@@ -45,12 +45,42 @@ def _run(cmd, verbose):
     subprocess.run([str(c) for c in cmd], check=True)
 
 
+UNITS = ["unit_core", "unit_scan", "unit_sort", "unit_by_key"]
+OBJDIR = PKG / "_build"
+
+
+def _unit_deps(unit: str):
+    """The unit file, the sources it includes, and every header."""
+    src = CSRC / f"{unit}.cu"
+    deps = [src] + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    for line in src.read_text().splitlines():
+        if line.startswith('#include "'):
+            deps.append(CSRC / line.split('"')[1])
+    return deps
+
+
 def build_library(force: bool = False, verbose: bool = False) -> Path:
-    deps = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
-    if force or _stale(LIB, deps):
+    """Compile the units as relocatable device code in parallel (only those
+    whose sources changed), then device-link them into liblcpp_b200.so."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    OBJDIR.mkdir(exist_ok=True)
+    objs = [OBJDIR / f"{u}.o" for u in UNITS]
+    todo = [(u, o) for u, o in zip(UNITS, objs) if force or _stale(o, _unit_deps(u))]
+
+    def compile_unit(uo):
+        u, o = uo
+        tmp = o.with_suffix(".o.tmp")
+        _run([_nvcc(), *NVCC_ARCH, "-lineinfo", "-O3", "-std=c++17", "-rdc=true", "-Xcompiler", "-fPIC",
+              f"-I{INCLUDE}", "-c", CSRC / f"{u}.cu", "-o", tmp], verbose)
+        os.replace(tmp, o)
+
+    with ThreadPoolExecutor(max_workers=len(UNITS)) as ex:
+        list(ex.map(compile_unit, todo))
+    if force or todo or _stale(LIB, objs):
         tmp = LIB.with_suffix(".so.tmp")
-        _run([_nvcc(), *NVCC_ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
-              "-shared", f"-I{INCLUDE}", CSRC / "lcpp_b200.cu", "-o", tmp], verbose)
+        _run([_nvcc(), *NVCC_ARCH, "-shared", "-rdc=true", "-Xcompiler", "-fPIC", *objs, "-o", tmp, "-ldl"],
+             verbose)
         os.replace(tmp, LIB)
     return LIB
 

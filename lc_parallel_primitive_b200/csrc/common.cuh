@@ -14,10 +14,10 @@ constexpr int WARP = 32;
 // ---------------------------------------------------------------------------
 // Device-side error word and look-back wait cap (one per device, per process).
 // ---------------------------------------------------------------------------
-// The library is built as one translation unit (lcpp_b200.cu), so these
-// definitions exist once.
-__device__ unsigned int g_error = 0;                 // first latched lcpp_status (as unsigned)
-__device__ unsigned int g_spin_limit = 1u << 22;     // polls before a wait gives up (~1 s)
+// Defined once, in runtime.cu; the units are compiled as relocatable device
+// code and device-linked into one library, so every kernel sees one copy.
+extern __device__ unsigned int g_error;        // first latched lcpp_status (as unsigned)
+extern __device__ unsigned int g_spin_limit;   // polls before a wait gives up (~1 s)
 
 __device__ __forceinline__ void set_error(int status) {
     atomicCAS(&g_error, 0u, (unsigned int)status);

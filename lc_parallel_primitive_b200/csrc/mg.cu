@@ -1,0 +1,661 @@
+// Multi-GPU primitives on one node over NCCL (one process per GPU): reduce,
+// scan with cross-GPU carries, and a global stable sort.  The reference has
+// no multi-GPU code; these extend its single-GPU entry points
+// (src/lcpp/device/device_reduce.h:169-185, device_scan.h:180-204,
+// device_radix_sort.h:129-153) to data sharded in rank order, and lift the
+// reference's 32-bit item count (device_radix_sort.h:136, details/scan.h:72).
+//
+// NCCL is resolved at run time (dlopen of libnccl.so.2; in a process that
+// already loaded NCCL, e.g. through PyTorch, that copy is reused), so the
+// library loads and its single-GPU entry points work on hosts without NCCL.
+// The communicator is the caller's ncclComm_t, passed as void*.
+//
+// Every entry point is asynchronous on the caller's stream except
+// lcpp_mg_sort, which waits once for the 2*G exchange counts (the sizes of
+// the NCCL send/receive calls must be known on the host).  Scratch comes from
+// the caller's temp buffer; nothing is allocated.
+//
+// Global sort, G ranks (ascending, stable over the concatenation of the
+// shards in rank order):
+//   1. each rank takes 4096 evenly spaced samples of its shard, as extended
+//      keys (order-preserving key image, rank << 32 | index) weighted by the
+//      shard size; NCCL all-gathers them (and all-reduces the global key
+//      min/max: bits above the highest differing bit are equal in every key
+//      and need no sorting).  The gathered samples are sorted on the device
+//      by this library's radix sort, and G-1 splitters are picked where the
+//      running weight crosses r/G.  Splitting on extended keys cuts runs of
+//      equal keys between ranks in input order, so every rank gets about
+//      n_total/G items whatever the key distribution.
+//   2. a bucket kernel gives every item its destination rank (number of
+//      splitters <= its extended key, one byte); one stable onesweep pass
+//      over those bytes groups the shard by destination.
+//   3. NCCL all-gather of the G bucket starts; this rank's send offsets and
+//      receive counts are copied to the host (the one synchronisation).
+//   4. grouped ncclSend/ncclRecv of keys and values; runs arrive in source
+//      rank order.
+//   5. local onesweep sort of the bits that differ, from the received runs
+//      into the caller's output.  Stable passes + rank-ordered runs keep
+//      equal keys in global input order.
+// Rank r ends with the r-th contiguous slice of the global order and its
+// length is returned.
+#include "common.cuh"
+#include <algorithm>
+#include <dlfcn.h>
+#include <nccl.h>
+#include <mutex>
+#include <vector>
+
+namespace lcpp {
+
+// ---------------------------------------------------------------------------
+// NCCL entry points, resolved once.
+// ---------------------------------------------------------------------------
+struct NcclApi {
+    bool ok = false;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommCount)(const ncclComm_t, int*) = nullptr;
+    ncclResult_t (*CommUserRank)(const ncclComm_t, int*) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+};
+
+static const NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        bool ok = true;
+        auto get = [&](auto& fp, const char* name) {
+            fp = reinterpret_cast<std::remove_reference_t<decltype(fp)>>(dlsym(h, name));
+            ok = ok && fp != nullptr;
+        };
+        get(api.GetUniqueId, "ncclGetUniqueId");
+        get(api.CommInitRank, "ncclCommInitRank");
+        get(api.CommDestroy, "ncclCommDestroy");
+        get(api.CommCount, "ncclCommCount");
+        get(api.CommUserRank, "ncclCommUserRank");
+        get(api.AllReduce, "ncclAllReduce");
+        get(api.AllGather, "ncclAllGather");
+        get(api.Send, "ncclSend");
+        get(api.Recv, "ncclRecv");
+        get(api.GroupStart, "ncclGroupStart");
+        get(api.GroupEnd, "ncclGroupEnd");
+        api.ok = ok;
+    });
+    return api;
+}
+
+#define MG_NCCL(call)                                         \
+    do {                                                      \
+        if ((call) != ncclSuccess) return LCPP_ERR_NCCL;      \
+    } while (0)
+#define MG_CUDA(call)                                         \
+    do {                                                      \
+        if ((call) != cudaSuccess) return LCPP_ERR_CUDA;      \
+    } while (0)
+
+static bool nccl_type(int dtype, ncclDataType_t& t) {
+    switch (dtype) {
+        case LCPP_I32: t = ncclInt32; return true;
+        case LCPP_U32: t = ncclUint32; return true;
+        case LCPP_F32: t = ncclFloat32; return true;
+        case LCPP_I64: t = ncclInt64; return true;
+        case LCPP_U64: t = ncclUint64; return true;
+        case LCPP_F64: t = ncclFloat64; return true;
+        default: return false;
+    }
+}
+
+static bool comm_shape(void* comm, int& rank, int& nranks) {
+    const NcclApi& A = nccl();
+    if (!A.ok || !comm) return false;
+    return A.CommCount((ncclComm_t)comm, &nranks) == ncclSuccess &&
+           A.CommUserRank((ncclComm_t)comm, &rank) == ncclSuccess && nranks > 0;
+}
+
+// ---------------------------------------------------------------------------
+// Small kernels
+// ---------------------------------------------------------------------------
+// carry = totals[0] (+) ... (+) totals[rank-1], in rank order (one thread:
+// G <= a few hundred), so every rank folds the same floats in the same order.
+template <typename T>
+__global__ void mg_carry_kernel(const T* totals, int rank, T* carry) {
+    T c = T(0);
+    for (int h = 0; h < rank; ++h) c = OpSum::apply<T>(c, totals[h]);
+    *carry = c;
+}
+
+// {min, ~max} of the ordered key image (min-reduction of both words gives the
+// global min and max).  Zero-length shards contribute the identity.
+template <typename KB, int KIND>
+__global__ void mg_minmax_kernel(const KB* keys, uint64_t n, unsigned long long* mm) {
+    unsigned long long lo = ~0ull, nhi = ~0ull;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const unsigned long long o = (unsigned long long)ordered_bits<KB, KIND, false>(keys[i]);
+        lo = o < lo ? o : lo;
+        nhi = ~o < nhi ? ~o : nhi;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const unsigned long long a = __shfl_xor_sync(0xffffffffu, lo, off);
+        const unsigned long long b = __shfl_xor_sync(0xffffffffu, nhi, off);
+        lo = a < lo ? a : lo;
+        nhi = b < nhi ? b : nhi;
+    }
+    if ((threadIdx.x & 31) == 0) {
+        atomicMin(mm, lo);
+        atomicMin(mm + 1, nhi);
+    }
+}
+
+// Bits that still differ from the global {min, ~max}: info[1] = hb + 1,
+// hb = highest bit where min and max differ (0: all keys equal).
+__global__ void mg_range_bits_kernel(const unsigned long long* gmm, uint32_t* info) {
+    const unsigned long long x = gmm[0] ^ ~gmm[1];
+    const int hb = x ? 63 - __clzll((long long)x) : -1;
+    info[0] = 0;
+    info[1] = (uint32_t)(hb + 1);
+}
+
+// Splitters are samples of the extended key (key image, position), position
+// = rank << 32 | local index: the global stable order is the lexicographic
+// order of extended keys, so equal keys are split between ranks in input
+// order and every rank gets an even share whatever the key distribution.
+constexpr int MG_SAMPLES = 4096;  // per rank
+
+// Sample i of this rank: the item at i * n / MG_SAMPLES, weighted by n (each
+// sample stands for n / MG_SAMPLES items).  Empty shards give weight-0
+// samples that sort last.
+template <typename KB, int KIND>
+__global__ void mg_sample_kernel(const KB* keys, uint64_t n, int me, uint64_t* skey, uint64_t* spos,
+                                 uint64_t* sw, uint32_t* sidx, int G) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < MG_SAMPLES) {
+        if (n) {
+            const uint64_t p = (uint64_t)i * n / MG_SAMPLES;
+            skey[i] = (uint64_t)ordered_bits<KB, KIND, false>(keys[p]);
+            spos[i] = ((uint64_t)me << 32) | p;
+            sw[i] = n;
+        } else {
+            skey[i] = ~0ull;
+            spos[i] = ~0ull;
+            sw[i] = 0;
+        }
+    }
+    // indices 0..G*MG_SAMPLES-1 for the sort of the gathered samples
+    for (int j = i; j < G * MG_SAMPLES; j += gridDim.x * blockDim.x) sidx[j] = (uint32_t)j;
+}
+
+// Splitter r (1..G-1) is the sample at which the running weight of the
+// sorted samples crosses r/G of the total: cum_excl <= target < cum_incl.
+__host__ __device__ inline uint64_t mg_target(uint64_t total, int r, int G) {
+    return (total / G) * r + (total % G) * r / G;
+}
+
+// One CTA of 1024 threads: sorted sample order `order`, weights sw; writes
+// G-1 splitter records {key, pos} to split (unused slots: {~0, ~0}).
+__global__ void __launch_bounds__(1024) mg_pick_splitters_kernel(const uint64_t* skey_sorted, const uint32_t* order,
+                                                                 const uint64_t* spos, const uint64_t* sw, int S,
+                                                                 int G, ulonglong2* split) {
+    __shared__ uint64_t s_part[1024];
+    const int t = threadIdx.x;
+    const int per = (S + 1023) / 1024;
+    const int lo = min(S, t * per), hi = min(S, lo + per);
+    uint64_t mine = 0;
+    for (int j = lo; j < hi; ++j) mine += sw[order[j]];
+    s_part[t] = mine;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {  // inclusive scan of the chunk sums
+        const uint64_t v = t >= o ? s_part[t - o] : 0;
+        __syncthreads();
+        s_part[t] += v;
+        __syncthreads();
+    }
+    const uint64_t total = s_part[1023];
+    for (int r = t; r < G - 1; r += 1024) split[r] = make_ulonglong2(~0ull, ~0ull);
+    __syncthreads();
+    uint64_t cum = t ? s_part[t - 1] : 0;
+    for (int j = lo; j < hi; ++j) {
+        const uint64_t w = sw[order[j]];
+        for (int r = 1; r < G; ++r) {
+            const uint64_t target = mg_target(total, r, G);
+            if (cum <= target && target < cum + w) split[r - 1] = make_ulonglong2(skey_sorted[j], spos[order[j]]);
+        }
+        cum += w;
+    }
+}
+
+// Bucket (destination rank) of every item: the number of splitters <= its
+// extended key, written as one byte per item.
+template <typename KB, int KIND>
+__global__ void mg_bucket_kernel(const KB* keys, uint64_t n, int me, const ulonglong2* split, int nsplit,
+                                 uint8_t* digits) {
+    __shared__ ulonglong2 s_split[256];
+    for (int i = threadIdx.x; i < nsplit; i += blockDim.x) s_split[i] = split[i];
+    __syncthreads();
+    const uint64_t rank_hi = (uint64_t)me << 32;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t o = (uint64_t)ordered_bits<KB, KIND, false>(ldcs(keys + i));
+        const uint64_t pos = rank_hi | i;
+        int lo = 0, hi = nsplit;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            const ulonglong2 sp = s_split[mid];
+            const bool le = sp.x < o || (sp.x == o && sp.y <= pos);
+            if (le) lo = mid + 1; else hi = mid;
+        }
+        digits[i] = (uint8_t)lo;
+    }
+}
+
+// Plan of this rank from the all-gathered digit starts (G rows of 257:
+// starts[0..255] of the rank's partition pass, then its n).  Bucket p goes
+// to rank p.  out (uint64): [0..G] send offsets into this rank's partitioned
+// shard, [G+1..2G] receive counts per source rank, [2G+1] = info[1].
+__global__ void mg_plan_kernel(const uint64_t* rows, int G, int me, const uint32_t* info, uint64_t* out) {
+    const uint64_t* mine = rows + (size_t)me * 257;
+    for (int p = threadIdx.x; p <= G; p += blockDim.x) out[p] = p < 256 ? mine[p] : mine[256];
+    for (int p = threadIdx.x; p < G; p += blockDim.x) {
+        const uint64_t* row = rows + (size_t)p * 257;
+        const uint64_t hi = me + 1 < 256 ? row[me + 1] : row[256];
+        out[G + 1 + p] = hi - row[me];
+    }
+    if (threadIdx.x == 0) out[2 * G + 1] = info[1];
+}
+
+// Row of this rank for the all-gather: the partition pass's digit starts
+// (uint32, in the sort's temp) widened, plus n.
+__global__ void mg_pack_starts_kernel(const uint32_t* starts, uint64_t n, uint64_t* row) {
+    const int t = threadIdx.x;
+    if (t < 256) row[t] = starts[t];
+    if (t == 0) row[256] = n;
+}
+
+// ---------------------------------------------------------------------------
+// Sort temp layout
+// ---------------------------------------------------------------------------
+struct MgSortLayout {
+    size_t mm, info, rows, plan, skey, spos, sw, sidx, skey_sorted, order, split, digits;
+    size_t part_k, part_v, recv_k, recv_v, sort, total;
+};
+
+static MgSortLayout mg_sort_layout(int kdt, int vdt, uint64_t n_local, uint64_t capacity, int G) {
+    MgSortLayout L{};
+    const size_t ks = lcpp_dtype_size(kdt);
+    const size_t vs = vdt == LCPP_NONE ? 0 : lcpp_dtype_size(vdt);
+    const size_t S = (size_t)G * MG_SAMPLES;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes, 256); return at; };
+    L.mm = take(4 * sizeof(unsigned long long));
+    L.info = take(2 * sizeof(uint32_t));
+    L.rows = take((size_t)G * 257 * sizeof(uint64_t));
+    L.plan = take((size_t)(2 * G + 2) * sizeof(uint64_t));
+    uint64_t m = n_local;
+    if (G > 1) {
+        L.skey = take(S * 8);
+        L.spos = take(S * 8);
+        L.sw = take(S * 8);
+        L.sidx = take(S * 4);
+        L.skey_sorted = take(S * 8);
+        L.order = take(S * 4);
+        L.split = take(256 * sizeof(ulonglong2));
+        L.digits = take(n_local);
+        L.part_k = take(n_local * ks);
+        L.part_v = take(n_local * vs);
+        L.recv_k = take(capacity * ks);
+        L.recv_v = take(capacity * vs);
+        m = std::max<uint64_t>(std::max<uint64_t>(capacity, n_local), S);
+    }
+    // one region serves, in turn, the sample sort, the partition pass and the final sort
+    const size_t big = lcpp_radix_sort_temp_bytes(kdt, vdt, m ? m : 1);
+    const size_t smp = G > 1 ? lcpp_radix_sort_temp_bytes(LCPP_U64, LCPP_U32, S) : 0;
+    L.sort = take(std::max(big, smp));
+    L.total = o;
+    return L;
+}
+
+static lcpp_status rs_sort_impl(int key_dtype, int value_dtype, int descending, const void* keys_in, void* keys_out,
+                                const void* values_in, void* values_out, uint64_t n, int begin_bit, int end_bit,
+                                void* temp, size_t temp_bytes, void* stream, const uint8_t* digits);
+
+}  // namespace lcpp
+
+using namespace lcpp;
+
+// ---------------------------------------------------------------------------
+// Communicator helpers (so that callers without their own NCCL binding, e.g.
+// Python over ctypes, can build a communicator).
+// ---------------------------------------------------------------------------
+extern "C" size_t lcpp_mg_unique_id_bytes(void) { return sizeof(ncclUniqueId); }
+
+extern "C" lcpp_status lcpp_mg_get_unique_id(void* id_out) {
+    const NcclApi& A = nccl();
+    if (!A.ok) return LCPP_ERR_NCCL;
+    if (!id_out) return LCPP_ERR_INVALID_ARG;
+    ncclUniqueId id;
+    MG_NCCL(A.GetUniqueId(&id));
+    memcpy(id_out, &id, sizeof(id));
+    return LCPP_OK;
+}
+
+extern "C" lcpp_status lcpp_mg_comm_init_rank(void** comm_out, int nranks, const void* id, int rank) {
+    const NcclApi& A = nccl();
+    if (!A.ok) return LCPP_ERR_NCCL;
+    if (!comm_out || !id || nranks <= 0 || rank < 0 || rank >= nranks) return LCPP_ERR_INVALID_ARG;
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof(uid));
+    ncclComm_t c = nullptr;
+    MG_NCCL(A.CommInitRank(&c, nranks, uid, rank));
+    *comm_out = (void*)c;
+    return LCPP_OK;
+}
+
+extern "C" lcpp_status lcpp_mg_comm_destroy(void* comm) {
+    const NcclApi& A = nccl();
+    if (!A.ok) return LCPP_ERR_NCCL;
+    if (!comm) return LCPP_ERR_INVALID_ARG;
+    MG_NCCL(A.CommDestroy((ncclComm_t)comm));
+    return LCPP_OK;
+}
+
+extern "C" lcpp_status lcpp_mg_comm_shape(void* comm, int* rank, int* nranks) {
+    if (!rank || !nranks) return LCPP_ERR_INVALID_ARG;
+    return comm_shape(comm, *rank, *nranks) ? LCPP_OK : LCPP_ERR_NCCL;
+}
+
+// ---------------------------------------------------------------------------
+// Reduce
+// ---------------------------------------------------------------------------
+extern "C" size_t lcpp_mg_reduce_temp_bytes(int dtype, uint64_t n_local) {
+    const size_t r = lcpp_reduce_temp_bytes(dtype, n_local);
+    return r ? 256 + r : 0;
+}
+
+extern "C" lcpp_status lcpp_mg_reduce(int op, int dtype, const void* in, void* out, uint64_t n_local,
+                                      void* temp, size_t temp_bytes, void* comm, void* stream) {
+    ncclDataType_t t;
+    if (!nccl_type(dtype, t) || op < 0 || op > 2 || !out || (n_local && !in)) return LCPP_ERR_INVALID_ARG;
+    const size_t need = lcpp_mg_reduce_temp_bytes(dtype, n_local);
+    if (!temp || temp_bytes < need) return LCPP_ERR_TEMP_TOO_SMALL;
+    int rank, G;
+    if (!comm_shape(comm, rank, G)) return LCPP_ERR_NCCL;
+    cudaStream_t s = (cudaStream_t)stream;
+    char* part = (char*)temp;  // this rank's partial (one element)
+    const lcpp_status st = lcpp_reduce(op, dtype, in, part, n_local, (char*)temp + 256, need - 256, stream);
+    if (st != LCPP_OK) return st;
+    const ncclRedOp_t rop = op == LCPP_OP_SUM ? ncclSum : op == LCPP_OP_MIN ? ncclMin : ncclMax;
+    ProfScope ps("mg_allreduce", s);
+    MG_NCCL(nccl().AllReduce(part, out, 1, t, rop, (ncclComm_t)comm, s));
+    return LCPP_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Scan
+// ---------------------------------------------------------------------------
+extern "C" size_t lcpp_mg_scan_temp_bytes(int dtype, uint64_t n_local, int nranks) {
+    const size_t es = lcpp_dtype_size(dtype);
+    const size_t sc = lcpp_scan_temp_bytes(dtype, n_local);
+    if (!es || !sc || nranks <= 0) return 0;
+    const size_t r = lcpp_reduce_temp_bytes(dtype, n_local);
+    // [total | carry | G totals][reduce temp][scan temp]
+    const size_t head = align_up(2 * 8 + (size_t)nranks * es, 256);
+    return head + align_up(r, 256) + sc;
+}
+
+extern "C" lcpp_status lcpp_mg_scan(int kind, int dtype, const void* in, void* out, uint64_t n_local,
+                                    void* temp, size_t temp_bytes, void* comm, void* stream) {
+    ncclDataType_t t;
+    if (!nccl_type(dtype, t) || (kind != LCPP_SCAN_EXCLUSIVE && kind != LCPP_SCAN_INCLUSIVE) ||
+        (n_local && (!in || !out)))
+        return LCPP_ERR_INVALID_ARG;
+    int rank, G;
+    if (!comm_shape(comm, rank, G)) return LCPP_ERR_NCCL;
+    const size_t need = lcpp_mg_scan_temp_bytes(dtype, n_local, G);
+    if (!need) return LCPP_ERR_INVALID_ARG;
+    if (!temp || temp_bytes < need) return LCPP_ERR_TEMP_TOO_SMALL;
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t es = lcpp_dtype_size(dtype);
+    char* base = (char*)temp;
+    char* total = base;
+    char* carry = base + 8;
+    char* totals = base + 16;
+    const size_t head = align_up(2 * 8 + (size_t)G * es, 256);
+    const size_t rt = align_up(lcpp_reduce_temp_bytes(dtype, n_local), 256);
+    char* rtemp = base + head;
+    char* stemp = rtemp + rt;
+    lcpp_status st;
+    {
+        ProfScope ps("mg_local_reduce", s);
+        st = lcpp_reduce(LCPP_OP_SUM, dtype, in, total, n_local, rtemp, rt, stream);
+    }
+    if (st != LCPP_OK) return st;
+    {
+        ProfScope ps("mg_allgather", s);
+        MG_NCCL(nccl().AllGather(total, totals, 1, t, (ncclComm_t)comm, s));
+        st = dispatch_dtype(dtype, [&](auto zero) -> lcpp_status {
+            using T = decltype(zero);
+            mg_carry_kernel<T><<<1, 1, 0, s>>>((const T*)totals, rank, (T*)carry);
+            count_launch();
+            return check_launch();
+        });
+    }
+    if (st != LCPP_OK) return st;
+    if (n_local == 0) return LCPP_OK;
+    ProfScope ps("mg_carry_scan", s);
+    return lcpp_scan_carry(kind, dtype, in, out, n_local, carry, stemp, temp_bytes - head - rt, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Global sort
+// ---------------------------------------------------------------------------
+extern "C" size_t lcpp_mg_sort_temp_bytes(int key_dtype, int value_dtype, uint64_t n_local, uint64_t capacity,
+                                          int nranks) {
+    if (nranks <= 0 || lcpp_radix_sort_temp_bytes(key_dtype, value_dtype, 1) == 0) return 0;
+    return mg_sort_layout(key_dtype, value_dtype, n_local, capacity, nranks).total;
+}
+
+extern "C" lcpp_status lcpp_mg_pick_splitters(const uint64_t* keys, const uint64_t* pos, const uint64_t* weights,
+                                               uint64_t count, int nranks, uint64_t* split_keys,
+                                               uint64_t* split_pos) {
+    if (!keys || !pos || !weights || !split_keys || !split_pos || nranks <= 0 || nranks > 256)
+        return LCPP_ERR_INVALID_ARG;
+    uint64_t total = 0;
+    for (uint64_t j = 0; j < count; ++j) total += weights[j];
+    for (int r = 0; r + 1 < nranks; ++r) split_keys[r] = split_pos[r] = ~0ull;
+    uint64_t cum = 0;
+    for (uint64_t j = 0; j < count; ++j) {
+        for (int r = 1; r < nranks; ++r) {
+            const uint64_t target = mg_target(total, r, nranks);
+            if (cum <= target && target < cum + weights[j]) {
+                split_keys[r - 1] = keys[j];
+                split_pos[r - 1] = pos[j];
+            }
+        }
+        cum += weights[j];
+    }
+    return LCPP_OK;
+}
+
+static int unsigned_view(size_t ks) { return ks == 4 ? LCPP_U32 : LCPP_U64; }
+
+extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* keys_in, const void* values_in,
+                                    uint64_t n_local, void* keys_out, void* values_out, uint64_t capacity,
+                                    uint64_t* n_out, void* temp, size_t temp_bytes, void* comm, void* stream) {
+    const int kind = key_kind(key_dtype);
+    const size_t ks = lcpp_dtype_size(key_dtype);
+    const size_t vs = value_dtype == LCPP_NONE ? 0 : lcpp_dtype_size(value_dtype);
+    if (kind < 0 || (value_dtype != LCPP_NONE && vs == 0) || !n_out) return LCPP_ERR_INVALID_ARG;
+    if ((n_local && !keys_in) || (vs && n_local && !values_in) || !keys_out || (vs && !values_out))
+        return LCPP_ERR_INVALID_ARG;
+    if (n_local >= (1ull << 32) || capacity >= (1ull << 32) || capacity < n_local) return LCPP_ERR_INVALID_ARG;
+    int me, G;
+    if (!comm_shape(comm, me, G)) return LCPP_ERR_NCCL;
+    if (G > 256) return LCPP_ERR_UNSUPPORTED;  // bucket ids are bytes
+    const MgSortLayout L = mg_sort_layout(key_dtype, value_dtype, n_local, capacity, G);
+    if (!temp || temp_bytes < L.total) return LCPP_ERR_TEMP_TOO_SMALL;
+    const NcclApi& A = nccl();
+    ncclComm_t c = (ncclComm_t)comm;
+    cudaStream_t s = (cudaStream_t)stream;
+    char* T = (char*)temp;
+    const size_t sort_bytes = L.total - L.sort;
+    *n_out = 0;
+
+    if (G == 1) {  // the local sort is the global sort
+        *n_out = n_local;
+        ProfScope ps("mg_local_sort", s);
+        return rs_sort_impl(key_dtype, value_dtype, 0, keys_in, keys_out, values_in, values_out, n_local, 0, 0,
+                            T + L.sort, sort_bytes, stream, nullptr);
+    }
+
+    unsigned long long* mm = (unsigned long long*)(T + L.mm);
+    uint32_t* info = (uint32_t*)(T + L.info);
+    const int S = G * MG_SAMPLES;
+    uint64_t* skey = (uint64_t*)(T + L.skey);
+    uint64_t* spos = (uint64_t*)(T + L.spos);
+    uint64_t* sw = (uint64_t*)(T + L.sw);
+    uint32_t* sidx = (uint32_t*)(T + L.sidx);
+    ulonglong2* split = (ulonglong2*)(T + L.split);
+    uint8_t* digits = (uint8_t*)(T + L.digits);
+    const DeviceInfo di = device_info();
+    const unsigned grid = (unsigned)std::min<uint64_t>(ceil_div(n_local ? n_local : 1, 1024), (uint64_t)di.sms * 4);
+    lcpp_status st;
+    // 1. global key range (bits that differ) and splitters from all ranks' samples
+    {
+        ProfScope ps("mg_splitters", s);
+        MG_CUDA(cudaMemsetAsync(mm, 0xFF, 2 * sizeof(unsigned long long), s));
+        auto go = [&](auto kb) -> lcpp_status {
+            using KB = decltype(kb);
+            const KB* k = (const KB*)keys_in;
+            const unsigned sg = (unsigned)ceil_div((uint64_t)MG_SAMPLES, 256);
+            switch (kind) {
+                case 0: mg_minmax_kernel<KB, 0><<<grid, 1024, 0, s>>>(k, n_local, mm);
+                        mg_sample_kernel<KB, 0><<<sg, 256, 0, s>>>(k, n_local, me, skey + (size_t)me * MG_SAMPLES,
+                                                                   spos + (size_t)me * MG_SAMPLES, sw + (size_t)me * MG_SAMPLES, sidx, G);
+                        break;
+                case 1: mg_minmax_kernel<KB, 1><<<grid, 1024, 0, s>>>(k, n_local, mm);
+                        mg_sample_kernel<KB, 1><<<sg, 256, 0, s>>>(k, n_local, me, skey + (size_t)me * MG_SAMPLES,
+                                                                   spos + (size_t)me * MG_SAMPLES, sw + (size_t)me * MG_SAMPLES, sidx, G);
+                        break;
+                default: mg_minmax_kernel<KB, 2><<<grid, 1024, 0, s>>>(k, n_local, mm);
+                         mg_sample_kernel<KB, 2><<<sg, 256, 0, s>>>(k, n_local, me, skey + (size_t)me * MG_SAMPLES,
+                                                                    spos + (size_t)me * MG_SAMPLES, sw + (size_t)me * MG_SAMPLES, sidx, G);
+                         break;
+            }
+            count_launch(2);
+            return check_launch();
+        };
+        st = ks == 4 ? go((uint32_t)0) : go((uint64_t)0);
+        if (st != LCPP_OK) return st;
+        MG_NCCL(A.GroupStart());
+        MG_NCCL(A.AllReduce(mm, mm + 2, 2, ncclUint64, ncclMin, c, s));
+        MG_NCCL(A.AllGather(skey + (size_t)me * MG_SAMPLES, skey, MG_SAMPLES, ncclUint64, c, s));
+        MG_NCCL(A.AllGather(spos + (size_t)me * MG_SAMPLES, spos, MG_SAMPLES, ncclUint64, c, s));
+        MG_NCCL(A.AllGather(sw + (size_t)me * MG_SAMPLES, sw, MG_SAMPLES, ncclUint64, c, s));
+        MG_NCCL(A.GroupEnd());
+        mg_range_bits_kernel<<<1, 1, 0, s>>>(mm + 2, info);
+        count_launch();
+        // samples are gathered rank-major, positions ascending: a stable sort by
+        // key leaves them in extended-key order
+        st = rs_sort_impl(LCPP_U64, LCPP_U32, 0, skey, T + L.skey_sorted, sidx, T + L.order, (uint64_t)S, 0, 0,
+                          T + L.sort, sort_bytes, stream, nullptr);
+        if (st != LCPP_OK) return st;
+        mg_pick_splitters_kernel<<<1, 1024, 0, s>>>((const uint64_t*)(T + L.skey_sorted), (const uint32_t*)(T + L.order),
+                                                    spos, sw, S, G, split);
+        count_launch();
+        if ((st = check_launch()) != LCPP_OK) return st;
+    }
+    // 2. bucket of every item, then one stable pass that groups the shard by bucket
+    char* pk = T + L.part_k;
+    char* pv = vs ? T + L.part_v : nullptr;
+    {
+        ProfScope ps("mg_partition", s);
+        if (n_local) {
+            auto go = [&](auto kb) -> lcpp_status {
+                using KB = decltype(kb);
+                const KB* k = (const KB*)keys_in;
+                switch (kind) {
+                    case 0: mg_bucket_kernel<KB, 0><<<grid, 1024, 0, s>>>(k, n_local, me, split, G - 1, digits); break;
+                    case 1: mg_bucket_kernel<KB, 1><<<grid, 1024, 0, s>>>(k, n_local, me, split, G - 1, digits); break;
+                    default: mg_bucket_kernel<KB, 2><<<grid, 1024, 0, s>>>(k, n_local, me, split, G - 1, digits); break;
+                }
+                count_launch();
+                return check_launch();
+            };
+            st = ks == 4 ? go((uint32_t)0) : go((uint64_t)0);
+            if (st != LCPP_OK) return st;
+            st = rs_sort_impl(unsigned_view(ks), value_dtype, 0, keys_in, pk, values_in, pv, n_local, 0, 8,
+                              T + L.sort, sort_bytes, stream, digits);
+            if (st != LCPP_OK) return st;
+        } else {
+            MG_CUDA(cudaMemsetAsync(T + L.sort, 0, 256 * sizeof(uint32_t), s));
+        }
+    }
+    // 3. all-gathered bucket starts -> exchange sizes -> host
+    std::vector<uint64_t> plan((size_t)2 * G + 2);
+    uint64_t* rows = (uint64_t*)(T + L.rows);
+    {
+        ProfScope ps("mg_plan", s);
+        // the partition pass leaves its 256 digit starts at the start of its temp (bins of pass 0)
+        mg_pack_starts_kernel<<<1, 256, 0, s>>>((const uint32_t*)(T + L.sort), n_local, rows + (size_t)me * 257);
+        count_launch();
+        if ((st = check_launch()) != LCPP_OK) return st;
+        MG_NCCL(A.AllGather(rows + (size_t)me * 257, rows, 257, ncclUint64, c, s));
+        mg_plan_kernel<<<1, 256, 0, s>>>(rows, G, me, info, (uint64_t*)(T + L.plan));
+        count_launch();
+        if ((st = check_launch()) != LCPP_OK) return st;
+        MG_CUDA(cudaMemcpyAsync(plan.data(), T + L.plan, plan.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
+    }
+    MG_CUDA(cudaStreamSynchronize(s));
+    const uint64_t* so = plan.data();
+    const uint64_t* rc = plan.data() + G + 1;
+    const int end_bit = (int)plan[2 * G + 1];
+    std::vector<uint64_t> ro(G + 1, 0);
+    for (int p = 0; p < G; ++p) ro[p + 1] = ro[p] + rc[p];
+    const uint64_t n_recv = ro[G];
+    if (n_recv > capacity) return LCPP_ERR_CAPACITY;
+    // 4. exchange (runs land in source-rank order)
+    char* rk = T + L.recv_k;
+    char* rv = vs ? T + L.recv_v : nullptr;
+    {
+        ProfScope ps("mg_exchange", s);
+        const uint64_t self = so[me + 1] - so[me];
+        if (self) {
+            MG_CUDA(cudaMemcpyAsync(rk + ro[me] * ks, pk + so[me] * ks, self * ks, cudaMemcpyDeviceToDevice, s));
+            if (vs) MG_CUDA(cudaMemcpyAsync(rv + ro[me] * vs, pv + so[me] * vs, self * vs, cudaMemcpyDeviceToDevice, s));
+        }
+        MG_NCCL(A.GroupStart());
+        for (int p = 0; p < G; ++p) {
+            if (p == me) continue;
+            const uint64_t sc = so[p + 1] - so[p];
+            if (sc) {
+                MG_NCCL(A.Send(pk + so[p] * ks, sc * ks, ncclUint8, p, c, s));
+                if (vs) MG_NCCL(A.Send(pv + so[p] * vs, sc * vs, ncclUint8, p, c, s));
+            }
+            if (rc[p]) {
+                MG_NCCL(A.Recv(rk + ro[p] * ks, rc[p] * ks, ncclUint8, p, c, s));
+                if (vs) MG_NCCL(A.Recv(rv + ro[p] * vs, rc[p] * vs, ncclUint8, p, c, s));
+            }
+        }
+        MG_NCCL(A.GroupEnd());
+    }
+    // 5. local sort of the bits that still differ
+    *n_out = n_recv;
+    if (n_recv == 0) return LCPP_OK;
+    ProfScope ps("mg_local_sort", s);
+    if (end_bit <= 0) {  // every key equal: arrival order is the stable order
+        MG_CUDA(cudaMemcpyAsync(keys_out, rk, n_recv * ks, cudaMemcpyDeviceToDevice, s));
+        if (vs) MG_CUDA(cudaMemcpyAsync(values_out, rv, n_recv * vs, cudaMemcpyDeviceToDevice, s));
+        return LCPP_OK;
+    }
+    return rs_sort_impl(key_dtype, value_dtype, 0, rk, keys_out, rv, values_out, n_recv, 0, end_bit, T + L.sort,
+                        sort_bytes, stream, nullptr);
+}

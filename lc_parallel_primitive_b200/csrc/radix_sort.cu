@@ -160,6 +160,34 @@ __global__ void __launch_bounds__(RS_DIGITS) rs_bins_scan_kernel(uint32_t* bins)
     b[threadIdx.x] = wpre + incl - c;
 }
 
+// Counts of precomputed one-byte digits (the DIG passes): lane-private
+// columns as above, 16 digits per 128-bit load.  bins[d] += count.
+__global__ void __launch_bounds__(HISTC_THREADS, 1)
+rs_digit_hist_kernel(const uint8_t* __restrict__ digits, uint64_t n, uint32_t* __restrict__ bins) {
+    __shared__ uint32_t hc[RS_DIGITS * 32];
+    for (uint32_t i = threadIdx.x; i < RS_DIGITS * 32; i += blockDim.x) hc[i] = 0;
+    __syncthreads();
+    const uint32_t col = threadIdx.x & 31;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t gtid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool aligned = (reinterpret_cast<uintptr_t>(digits) & 15) == 0;
+    const uint64_t nvec = aligned ? n / 16 : 0;
+    for (uint64_t i = gtid; i < nvec; i += stride) {
+        const uint4 q = ld_stream(reinterpret_cast<const uint4*>(digits) + i);
+        const uint8_t* e = reinterpret_cast<const uint8_t*>(&q);
+#pragma unroll
+        for (int v = 0; v < 16; ++v) atomicAdd(&hc[e[v] * 32 + col], 1u);
+    }
+    for (uint64_t t = nvec * 16 + gtid; t < n; t += stride) atomicAdd(&hc[digits[t] * 32 + col], 1u);
+    __syncthreads();
+    for (uint32_t b = threadIdx.x; b < RS_DIGITS; b += blockDim.x) {
+        uint32_t sum = 0;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) sum += hc[b * 32 + ((c + b) & 31)];
+        if (sum) atomicAdd(bins + b, sum);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Look-back words: {INCLUSIVE | PARTIAL | count} in 32 or 64 bits.
 // ---------------------------------------------------------------------------
@@ -186,12 +214,13 @@ struct RsPass {
     const uint32_t* bins;   // 256 global digit starts of this pass
     void* lookback;         // tiles x 256 words, zeroed
     uint32_t* ticket;       // zeroed
+    const uint8_t* digits;      // DIG kernels: precomputed digit of every item (no key bits used)
 };
 
-template <typename KB, typename VB, int THREADS>
+template <typename KB, typename VB, int THREADS, bool DIG = false>
 constexpr size_t rs_smem_bytes() {
     constexpr int TILE = THREADS * RsItems<KB>::value;
-    return (size_t)TILE * sizeof(KB) +
+    return (DIG ? (size_t)TILE : 0) + (size_t)TILE * sizeof(KB) +
            (std::is_same<VB, NoValue>::value ? 0 : (size_t)TILE * sizeof(VB)) +
            (size_t)(THREADS / 32) * RS_DIGITS * 4 * 2 + RS_DIGITS * 4 * 2 + 64;
 }
@@ -203,7 +232,7 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-template <typename KB, typename VB, typename W, int KIND, bool DESC, int THREADS>
+template <typename KB, typename VB, typename W, int KIND, bool DESC, int THREADS, bool DIG = false>
 __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(RsPass a) {
     constexpr int RS_WARPS = THREADS / 32;
     constexpr int ITEMS = RsItems<KB>::value;
@@ -220,6 +249,7 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     uint32_t* s_gbase = s_wc + RS_WARPS * RS_DIGITS;         // [256]
     uint32_t* s_misc = s_gbase + RS_DIGITS;                  // [0] tile id, [1..8] warp sums
     uint32_t* s_wm = s_misc + 16;                            // [RS_WARPS][256] lane masks per digit
+    uint8_t* s_dig = reinterpret_cast<uint8_t*>(s_wm + RS_WARPS * RS_DIGITS);  // DIG: digit per tile slot
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) s_misc[0] = atomicAdd(a.ticket, 1u);
@@ -240,6 +270,18 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
         const uint32_t li = wbase + i * 32 + lane;
         key[i] = li < num_valid ? ldcs(kin + tile_base + li) : KB(0);
     }
+    uint32_t dg[DIG ? ITEMS : 1];
+    if constexpr (DIG) {
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {
+            const uint32_t li = wbase + i * 32 + lane;
+            dg[i] = li < num_valid ? (uint32_t)__ldcs(a.digits + tile_base + li) : (RS_DIGITS - 1);
+        }
+    }
+    auto digit_at = [&](int i, uint32_t li) -> uint32_t {
+        if constexpr (DIG) return dg[i];
+        else return li < num_valid ? digit_of<KB, KIND, DESC>(key[i], a.shift, a.mask) : (RS_DIGITS - 1);
+    };
     // ---- values of a full tile: asynchronous copy into shared memory (input
     // order) that lands while the keys are ranked ------------------------------
     const VB* vin = reinterpret_cast<const VB*>(a.vals_in);
@@ -262,7 +304,7 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
         const uint32_t li = wbase + i * 32 + lane;
-        const uint32_t d = li < num_valid ? digit_of<KB, KIND, DESC>(key[i], a.shift, a.mask) : (RS_DIGITS - 1);
+        const uint32_t d = digit_at(i, li);
         atomicAdd(wc + d, 1u);
     }
     __syncthreads();
@@ -350,7 +392,7 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
         const uint32_t li = wbase + i * 32 + lane;
-        const uint32_t d = li < num_valid ? digit_of<KB, KIND, DESC>(key[i], a.shift, a.mask) : (RS_DIGITS - 1);
+        const uint32_t d = digit_at(i, li);
         // Lanes holding the same digit: each lane sets its bit in the warp's
         // mask word for its digit, reads the word back, and the highest lane
         // of the group advances the warp's running position and clears the word.
@@ -369,6 +411,7 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
         __syncwarp();
         pos[i] = old + __popc(peers & lt);
         s_keys[pos[i]] = key[i];
+        if constexpr (DIG) s_dig[pos[i]] = (uint8_t)d;
     }
 
     // ---- values into shared memory in digit order -----------------------------
@@ -403,7 +446,9 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
         const uint32_t idx = i * THREADS + tid;
         if (idx < num_valid) {
             const KB k = s_keys[idx];
-            const uint32_t d = digit_of<KB, KIND, DESC>(k, a.shift, a.mask);
+            uint32_t d;
+            if constexpr (DIG) d = s_dig[idx];
+            else d = digit_of<KB, KIND, DESC>(k, a.shift, a.mask);
             const uint32_t g = s_gbase[d] + idx;
             stcs(kout + g, k);
             if constexpr (HAS_V) stcs(vout + g, s_vals[idx]);
@@ -459,7 +504,7 @@ static int key_kind(int dtype) {
 template <typename KB, typename VB, typename W, int KIND, bool DESC>
 static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out, const void* vals_in,
                           void* vals_out, uint64_t n, uint32_t begin_bit, uint32_t end_bit, char* temp,
-                          cudaStream_t s) {
+                          cudaStream_t s, const uint8_t* digits) {
     uint32_t* bins = (uint32_t*)(temp + L.bins_off);
     uint32_t* tickets = (uint32_t*)(temp + L.ticket_off);
     char* lb = temp + L.lb_off;
@@ -480,15 +525,29 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
         if (cudaFuncSetAttribute(hk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hsmem) != cudaSuccess)
             return LCPP_ERR_CUDA;
         { ProfScope ps("rs_histogram", s);
-        hk<<<(unsigned)g, HISTC_THREADS, hsmem, s>>>((const KB*)keys_in, n, bins, begin_bit, end_bit, L.passes); }
+        if (digits)
+            rs_digit_hist_kernel<<<(unsigned)g, HISTC_THREADS, 0, s>>>(digits, n, bins);
+        else
+            hk<<<(unsigned)g, HISTC_THREADS, hsmem, s>>>((const KB*)keys_in, n, bins, begin_bit, end_bit, L.passes); }
         { ProfScope ps("rs_bins_scan", s);
         rs_bins_scan_kernel<<<L.passes, RS_DIGITS, 0, s>>>(bins); }
         count_launch(2);
     }
-    const int threads = rs_threads();
-    const size_t smem = threads == 256 ? rs_smem_bytes<KB, VB, 256>() : rs_smem_bytes<KB, VB, RS_THREADS>();
-    auto kern = threads == 256 ? rs_onesweep_kernel<KB, VB, W, KIND, DESC, 256>
-                               : rs_onesweep_kernel<KB, VB, W, KIND, DESC, RS_THREADS>;
+    const int threads = digits ? RS_THREADS : rs_threads();
+    size_t smem;
+    void (*kern)(RsPass);
+    if (digits) {  // one pass over precomputed digits (only unsigned ascending instantiations)
+        if constexpr (KIND == 0 && !DESC) {
+            smem = rs_smem_bytes<KB, VB, RS_THREADS, true>();
+            kern = rs_onesweep_kernel<KB, VB, W, 0, false, RS_THREADS, true>;
+        } else {
+            return LCPP_ERR_INVALID_ARG;
+        }
+    } else {
+        smem = threads == 256 ? rs_smem_bytes<KB, VB, 256>() : rs_smem_bytes<KB, VB, RS_THREADS>();
+        kern = threads == 256 ? rs_onesweep_kernel<KB, VB, W, KIND, DESC, 256>
+                              : rs_onesweep_kernel<KB, VB, W, KIND, DESC, RS_THREADS>;
+    }
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return LCPP_ERR_CUDA;
 
@@ -513,6 +572,7 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
         a.bins = bins + p * RS_DIGITS;
         a.lookback = lb + (size_t)p * L.tiles * RS_DIGITS * L.lb_word;
         a.ticket = tickets + p;
+        a.digits = digits;
         { ProfScope ps("rs_onesweep", s);
         kern<<<(unsigned)L.tiles, threads, smem, s>>>(a); }
         count_launch();
@@ -525,22 +585,23 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
 
 template <typename KB, typename VB, int KIND>
 static lcpp_status rs_dispatch_w(const RsLayout& L, bool desc, const void* ki, void* ko, const void* vi,
-                                 void* vo, uint64_t n, uint32_t bb, uint32_t eb, char* t, cudaStream_t s) {
+                                 void* vo, uint64_t n, uint32_t bb, uint32_t eb, char* t, cudaStream_t s,
+                                 const uint8_t* sd) {
     if (L.lb_word == 4)
-        return desc ? rs_run<KB, VB, uint32_t, KIND, true>(L, ki, ko, vi, vo, n, bb, eb, t, s)
-                    : rs_run<KB, VB, uint32_t, KIND, false>(L, ki, ko, vi, vo, n, bb, eb, t, s);
-    return desc ? rs_run<KB, VB, uint64_t, KIND, true>(L, ki, ko, vi, vo, n, bb, eb, t, s)
-                : rs_run<KB, VB, uint64_t, KIND, false>(L, ki, ko, vi, vo, n, bb, eb, t, s);
+        return desc ? rs_run<KB, VB, uint32_t, KIND, true>(L, ki, ko, vi, vo, n, bb, eb, t, s, sd)
+                    : rs_run<KB, VB, uint32_t, KIND, false>(L, ki, ko, vi, vo, n, bb, eb, t, s, sd);
+    return desc ? rs_run<KB, VB, uint64_t, KIND, true>(L, ki, ko, vi, vo, n, bb, eb, t, s, sd)
+                : rs_run<KB, VB, uint64_t, KIND, false>(L, ki, ko, vi, vo, n, bb, eb, t, s, sd);
 }
 
 template <typename KB, typename VB>
 static lcpp_status rs_dispatch_kind(int kind, const RsLayout& L, bool desc, const void* ki, void* ko,
                                     const void* vi, void* vo, uint64_t n, uint32_t bb, uint32_t eb,
-                                    char* t, cudaStream_t s) {
+                                    char* t, cudaStream_t s, const uint8_t* sd) {
     switch (kind) {
-        case 0: return rs_dispatch_w<KB, VB, 0>(L, desc, ki, ko, vi, vo, n, bb, eb, t, s);
-        case 1: return rs_dispatch_w<KB, VB, 1>(L, desc, ki, ko, vi, vo, n, bb, eb, t, s);
-        default: return rs_dispatch_w<KB, VB, 2>(L, desc, ki, ko, vi, vo, n, bb, eb, t, s);
+        case 0: return rs_dispatch_w<KB, VB, 0>(L, desc, ki, ko, vi, vo, n, bb, eb, t, s, sd);
+        case 1: return rs_dispatch_w<KB, VB, 1>(L, desc, ki, ko, vi, vo, n, bb, eb, t, s, sd);
+        default: return rs_dispatch_w<KB, VB, 2>(L, desc, ki, ko, vi, vo, n, bb, eb, t, s, sd);
     }
 }
 
@@ -564,11 +625,17 @@ extern "C" size_t lcpp_radix_sort_temp_bytes(int key_dtype, int value_dtype, uin
     return rs_layout(ks, vs, n, (uint32_t)(ks * 8 / RS_BITS)).total;
 }
 
-extern "C" lcpp_status lcpp_radix_sort(int key_dtype, int value_dtype, int descending,
-                                       const void* keys_in, void* keys_out,
-                                       const void* values_in, void* values_out, uint64_t n,
-                                       int begin_bit, int end_bit,
-                                       void* temp, size_t temp_bytes, void* stream) {
+namespace lcpp {
+// Body of lcpp_radix_sort.  digits (device pointer or NULL): one pass that
+// orders the items by a precomputed one-byte digit per item instead of key
+// bits (stable); the multi-GPU sort partitions its shards by splitter bucket
+// this way.  Needs begin_bit = 0, end_bit <= 8 and is served for unsigned
+// ascending key views only (the caller passes keys as raw unsigned bits).
+static lcpp_status rs_sort_impl(int key_dtype, int value_dtype, int descending,
+                                const void* keys_in, void* keys_out,
+                                const void* values_in, void* values_out, uint64_t n,
+                                int begin_bit, int end_bit,
+                                void* temp, size_t temp_bytes, void* stream, const uint8_t* digits) {
     const int kind = key_kind(key_dtype);
     if (kind < 0) return LCPP_ERR_INVALID_ARG;
     const size_t ks = lcpp_dtype_size(key_dtype);
@@ -586,14 +653,25 @@ extern "C" lcpp_status lcpp_radix_sort(int key_dtype, int value_dtype, int desce
     char* t = (char*)temp;
     const bool desc = descending != 0;
     const uint32_t bb = (uint32_t)begin_bit, eb = (uint32_t)end_bit;
+    const uint8_t* sd = digits;
     if (ks == 4) {
-        if (vs == 0) return rs_dispatch_kind<uint32_t, NoValue>(kind, L, desc, keys_in, keys_out, nullptr, nullptr, n, bb, eb, t, s);
-        if (vs == 4) return rs_dispatch_kind<uint32_t, uint32_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
-        return rs_dispatch_kind<uint32_t, uint64_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
+        if (vs == 0) return rs_dispatch_kind<uint32_t, NoValue>(kind, L, desc, keys_in, keys_out, nullptr, nullptr, n, bb, eb, t, s, sd);
+        if (vs == 4) return rs_dispatch_kind<uint32_t, uint32_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s, sd);
+        return rs_dispatch_kind<uint32_t, uint64_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s, sd);
     }
-    if (vs == 0) return rs_dispatch_kind<uint64_t, NoValue>(kind, L, desc, keys_in, keys_out, nullptr, nullptr, n, bb, eb, t, s);
-    if (vs == 4) return rs_dispatch_kind<uint64_t, uint32_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
-    return rs_dispatch_kind<uint64_t, uint64_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s);
+    if (vs == 0) return rs_dispatch_kind<uint64_t, NoValue>(kind, L, desc, keys_in, keys_out, nullptr, nullptr, n, bb, eb, t, s, sd);
+    if (vs == 4) return rs_dispatch_kind<uint64_t, uint32_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s, sd);
+    return rs_dispatch_kind<uint64_t, uint64_t>(kind, L, desc, keys_in, keys_out, values_in, values_out, n, bb, eb, t, s, sd);
+}
+}  // namespace lcpp
+
+extern "C" lcpp_status lcpp_radix_sort(int key_dtype, int value_dtype, int descending,
+                                       const void* keys_in, void* keys_out,
+                                       const void* values_in, void* values_out, uint64_t n,
+                                       int begin_bit, int end_bit,
+                                       void* temp, size_t temp_bytes, void* stream) {
+    return rs_sort_impl(key_dtype, value_dtype, descending, keys_in, keys_out, values_in, values_out, n,
+                        begin_bit, end_bit, temp, temp_bytes, stream, nullptr);
 }
 
 // ---------------------------------------------------------------------------

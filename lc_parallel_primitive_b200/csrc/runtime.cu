@@ -5,6 +5,9 @@
 
 namespace lcpp {
 
+__device__ unsigned int g_error = 0;
+__device__ unsigned int g_spin_limit = 1u << 22;
+
 
 DeviceInfo device_info() {
     static std::mutex mu;
@@ -38,6 +41,7 @@ extern "C" const char* lcpp_status_string(lcpp_status s) {
         case LCPP_ERR_LOOKBACK_TIMEOUT: return "look-back wait timed out";
         case LCPP_ERR_NCCL: return "NCCL error";
         case LCPP_ERR_UNSUPPORTED: return "unsupported";
+        case LCPP_ERR_CAPACITY: return "output capacity exceeded";
         default: return "unknown status";
     }
 }
@@ -66,6 +70,17 @@ extern "C" lcpp_status lcpp_set_spin_limit(uint32_t iterations) {
     const unsigned int v = iterations ? iterations : (1u << 22);
     if (cudaMemcpyToSymbol(g_spin_limit, &v, sizeof(v)) != cudaSuccess) return LCPP_ERR_CUDA;
     return LCPP_OK;
+}
+
+namespace lcpp {
+// Compiled with the same flags as every kernel of the library.
+__global__ void lcpp_arch_probe_kernel() {}
+}  // namespace lcpp
+
+extern "C" int lcpp_kernel_binary_version(void) {
+    cudaFuncAttributes a{};
+    if (cudaFuncGetAttributes(&a, lcpp_arch_probe_kernel) != cudaSuccess) return LCPP_ERR_CUDA;
+    return a.binaryVersion;
 }
 
 extern "C" uint64_t lcpp_kernel_launch_count(void) { return g_launches.load(); }

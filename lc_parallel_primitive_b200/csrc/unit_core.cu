@@ -1,0 +1,5 @@
+// Compilation unit of liblcpp_b200.so (relocatable device code): Reduce, ArgMin/ArgMax, segment reduce and the library-wide state.
+#include "runtime.cu"
+#include "reduce.cu"
+#include "segment_reduce.cu"
+#include "arg_reduce.cu"
