@@ -123,13 +123,13 @@ def run_reference_arm(args, rank, world):
     """CPU path of the reference algorithm on the host cores (rank 0 only)."""
     if rank != 0:
         return 0
-    import oracle
-    from lc_parallel_primitive_b200 import datagen as G
+    import oracle  # the reference algorithm's CPU restatement; nothing of the package is loaded here
 
     cores = os.cpu_count() or 1
     sample = 1 << 24  # bounded sample of the 2^28-pair workload per step
-    keys = G.u32(sample, seed=1, stream=7)
-    vals = G.iota_u32(sample)
+    rng = np.random.Generator(np.random.PCG64(1))
+    keys = rng.integers(0, 1 << 32, size=sample, dtype=np.uint64).astype(np.uint32)  # uniform over 2^32
+    vals = np.arange(sample, dtype=np.uint32)
     for _ in range(max(args.warmup, 1)):
         oracle.radix_sort(keys, vals, threads=cores)
     times = []
@@ -142,10 +142,11 @@ def run_reference_arm(args, rank, world):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u32", "data": "synthetic (PCG32 seeded)",
+        "scaling": "weak", "vs_baseline": None, "dtype": "u32", "data": "synthetic (numpy PCG64 seeded)",
         "config": {"workload": "SortPairs u32 keys (uniform 2^32) + u32 iota values, BASELINE config 3",
                    "n_per_step": sample, "note": "reference CPU path = oracle/ LSD radix sort restatement "
-                   "(LuisaCompute, the reference's runtime, is absent: reference not buildable)"},
+                   "(LuisaCompute, the reference's runtime, is absent: reference not buildable); the rate is "
+                   "per pair over a 2^24-pair sample of the 2^28-pair step (numpy PCG64 inputs, same distribution)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"{sample} pairs per step (bounded sample of 2^28)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -165,6 +166,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end timing")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--n-log2", type=int, default=28, help="pairs per GPU = 2^n (profiling runs use less)")
+    ap.add_argument("--no-mg", action="store_true", help="skip the config-5 multi-GPU lines")
+    ap.add_argument("--mg-scale", type=int, default=0, help="shrink the config-5 inputs by 2^k (tests)")
     ap.add_argument("--extras-scale", type=int, default=0,
                     help="shrink the scan/reduce/segment inputs by 2^k (profiling runs)")
     args = ap.parse_args()
@@ -212,17 +215,25 @@ def main():
     d_temp = torch.empty(tb, dtype=torch.uint8, device=dev)
 
     mg_state = {}
+    if world > 1:  # global sort through the multi-GPU C ABI, buffers allocated once
+        from lc_parallel_primitive_b200 import multi_gpu as M
+
+        comm = M.comm_for()
+        cap = M.default_capacity(n)
+        mg_ko = torch.empty(cap, dtype=torch.uint32, device=dev)
+        mg_vo = torch.empty(cap, dtype=torch.uint32, device=dev)
+        del d_temp
+        d_temp = torch.empty(M.mg_sort_temp_bytes(d_keys.view(torch.uint32), d_vals.view(torch.uint32), cap, world),
+                             dtype=torch.uint8, device=dev)
 
     def sort_once():
         if world == 1:
             L.check(lib.lcpp_radix_sort(L.U32, L.U32, 0, d_keys.data_ptr(), d_keys_out.data_ptr(),
                                         d_vals.data_ptr(), d_vals_out.data_ptr(), n, 0, 0, d_temp.data_ptr(), tb,
                                         sh), "sort")
-        else:  # global sort across the ranks: local sort, splitters, all-to-all, final local sort
-            from lc_parallel_primitive_b200.multi_gpu import mg_sort_pairs
-
-            r = mg_sort_pairs(d_keys.view(torch.uint32), d_vals.view(torch.uint32))
-            mg_state["res"] = r
+        else:  # sampled splitters, partition pass, NCCL exchange, local sort
+            mg_state["res"] = M.mg_sort_pairs(d_keys.view(torch.uint32), d_vals.view(torch.uint32), comm=comm,
+                                              capacity=cap, temp=d_temp, keys_out=mg_ko, vals_out=mg_vo)
 
     for _ in range(args.warmup):
         sort_once()
@@ -246,7 +257,9 @@ def main():
         torch.distributed.all_gather(allends, ends)
         e = torch.stack(allends).cpu().tolist()
         assert all(e[i][1] <= e[i + 1][0] for i in range(world - 1) if e[i][1] >= 0 and e[i + 1][0] >= 0)
-        assert sum(r.counts_per_rank) == world * n
+        cnt = torch.tensor([r.n], dtype=torch.int64, device=dev)
+        torch.distributed.all_reduce(cnt)
+        assert int(cnt.item()) == world * n
         del k
         mg_state.clear()
     torch.cuda.empty_cache()
@@ -298,7 +311,8 @@ def main():
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_keys, d_vals,
-                      d_keys_out, d_vals_out, d_temp, args, barrier, max_over_ranks)
+                      d_keys_out, d_vals_out, d_temp, args, barrier, max_over_ranks,
+                      mg_sort=(lambda: (sort_once(), mg_state["res"])[1]) if world > 1 else None)
 
     # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------
     cpu = None
@@ -318,6 +332,10 @@ def main():
     if not args.no_extras:
         del h_keys_out, h_vals_out
         extras = run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier, args.extras_scale)
+    if not args.no_mg:
+        del d_keys, d_vals, d_keys_out, d_vals_out, d_temp, mg_state
+        torch.cuda.empty_cache()
+        extras.update(run_mg_extras(torch, dev, lib, L, peak, rank, world, max_over_ranks, barrier, args.mg_scale))
 
     if rank == 0:
         line = {
@@ -325,8 +343,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u32", "data": "synthetic (PCG32 seeded, uniform u32 keys, iota values)",
             "config": {"workload": f"DeviceRadixSort::SortPairs, n=2^{args.n_log2} u32 keys + u32 values per GPU (BASELINE config 3)"
-                       + ("" if world == 1 else "; global sort over all GPUs (local onesweep, sampled splitters, NCCL all-to-all, final onesweep)"),
-                       "n_per_gpu": n, "parallelism": f"global sort x{world} (torch.distributed NCCL all_to_all)" if world > 1 else "single GPU",
+                       + ("" if world == 1 else "; global sort over all GPUs (lcpp_mg_sort: sampled extended-key splitters, one onesweep partition pass, NCCL send/recv exchange, local onesweep sort)"),
+                       "n_per_gpu": n, "parallelism": f"global sort x{world} (NCCL point-to-point exchange in lcpp_mg_sort)" if world > 1 else "single GPU",
                        "l2": "inputs 2 GiB per step > 126 MB L2 (no flush needed)",
                        "algorithmic_bytes_per_pair": 68},
             "roofline": {"bound": "hbm", "kernel": "rs_onesweep_kernel (one 8-bit pass)",
@@ -350,7 +368,7 @@ def main():
 
 
 def run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_keys, d_vals, d_keys_out,
-            d_vals_out, d_temp, args, barrier, max_over_ranks):
+            d_vals_out, d_temp, args, barrier, max_over_ranks, mg_sort=None):
     """Same metric through the public API (DeviceRadixSort.SortPairs recorded
     into a CommandList and committed to a Stream), with every step's inputs
     copied from pinned host memory and its sorted pairs copied back.  The
@@ -363,8 +381,6 @@ def run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_k
     sorter.create(None)
     e2e_steps = max(3, min(6, args.steps))
     if world > 1:  # the multi-GPU entry point; this rank's slice of the result comes back
-        from lc_parallel_primitive_b200.multi_gpu import mg_sort_pairs
-
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize()
@@ -373,7 +389,7 @@ def run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_k
         for _ in range(e2e_steps):
             d_keys.copy_(h_keys, non_blocking=True)
             d_vals.copy_(h_vals, non_blocking=True)
-            r = mg_sort_pairs(d_keys.view(torch.uint32), d_vals.view(torch.uint32))
+            r = mg_sort()
             m = min(r.keys.numel(), h_keys_out.numel())
             h_keys_out[:m].copy_(r.keys.view(torch.int32)[:m], non_blocking=True)
             h_vals_out[:m].copy_(r.values.view(torch.int32)[:m], non_blocking=True)
@@ -383,7 +399,7 @@ def run_e2e(torch, stream, n, world, h_keys, h_vals, h_keys_out, h_vals_out, d_k
         barrier()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
         return {"value": world * n / (e2e_ms * 1e-3) / 1e9, "unit": UNIT, "h2d_bytes_per_step": 8 * n,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "api": "multi_gpu.mg_sort_pairs",
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "api": "multi_gpu.mg_sort_pairs (lcpp_mg_sort)",
                 "steps": e2e_steps}
 
     dev = d_keys.device
@@ -518,6 +534,36 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
     byts = 4 * N + 4 * (S + 1) + 4 * S  # values + CSR offsets + outputs
     out[f"segment_sum_f32_2p{27 - shrink}_2p{20 - shrink}"] = {"ms": ms, "GB/s": byts / ms / 1e6,
                                                               "frac": byts / ms / 1e6 / peak, **kern}
+    # segment Max over int32 (full range), same segmentation (config 4b)
+    xi = torch.from_numpy(G.u32(N, seed=1, stream=13).view(np.int32)).to(dev)
+    oi = torch.empty(S, dtype=torch.int32, device=dev)
+    ms = timeit(lambda: L.check(lib.lcpp_segment_reduce(2, L.I32, xi.data_ptr(), oi.data_ptr(), S, b.data_ptr(),
+                                                        e.data_ptr(), t.data_ptr(), tb, sh)), 20)
+    out[f"segment_max_i32_2p{27 - shrink}_2p{20 - shrink}"] = {"ms": ms, "GB/s": byts / ms / 1e6,
+                                                              "frac": byts / ms / 1e6 / peak}
+    del xi, oi, xs
+
+    # SortKeys (config 3a, 36 B/key) and the skewed SortPairs (config 3c, keys & 0xFF, 68 B/pair schedule)
+    n = 1 << (28 - shrink)
+    k = torch.from_numpy(G.u32(n, seed=2, stream=7).view(np.int32)).to(dev)
+    ko = torch.empty_like(k)
+    tbk = lib.lcpp_radix_sort_temp_bytes(L.U32, L.NONE, n)
+    tk = torch.empty(tbk, dtype=torch.uint8, device=dev)
+    ms = timeit(lambda: L.check(lib.lcpp_radix_sort(L.U32, L.NONE, 0, k.data_ptr(), ko.data_ptr(), None, None, n,
+                                                    0, 0, tk.data_ptr(), tbk, sh)), 10)
+    out[f"sort_keys_u32_2p{28 - shrink}"] = {"ms": ms, "Gkeys/s": n / ms / 1e6, "GB/s": 36 * n / ms / 1e6,
+                                              "frac": 36 * n / ms / 1e6 / peak}
+    del tk
+    ks = torch.from_numpy(G.u32_masked(n, 0xFF, seed=3).view(np.int32)).to(dev)
+    v = torch.arange(n, dtype=torch.int32, device=dev)
+    vo = torch.empty_like(v)
+    tbp = lib.lcpp_radix_sort_temp_bytes(L.U32, L.U32, n)
+    tp = torch.empty(tbp, dtype=torch.uint8, device=dev)
+    ms = timeit(lambda: L.check(lib.lcpp_radix_sort(L.U32, L.U32, 0, ks.data_ptr(), ko.data_ptr(), v.data_ptr(),
+                                                    vo.data_ptr(), n, 0, 0, tp.data_ptr(), tbp, sh)), 10)
+    out[f"sort_pairs_skewed8_u32_2p{28 - shrink}"] = {"ms": ms, "Gpairs/s": n / ms / 1e6, "GB/s": 68 * n / ms / 1e6,
+                                                      "frac": 68 * n / ms / 1e6 / peak}
+    del k, ko, ks, v, vo, tp
 
     # scan-by-key / reduce-by-key: 2^28 int32 keys in runs of mean length 100, int32 values
     n = 1 << (28 - shrink)
@@ -541,6 +587,177 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
     byts = 8 * n + 8 * runs
     out[f"reduce_by_key_sum_i32_2p{28 - shrink}"] = {"ms": ms, "GB/s": byts / ms / 1e6, "frac": byts / ms / 1e6 / peak,
                                                      "runs": runs}
+    return out
+
+
+def _fill_u64_uniform(torch, out, gen):
+    """Uniform 64-bit keys written into out (int64 view) in chunks."""
+    chunk = 1 << 26
+    for i in range(0, out.numel(), chunk):
+        m = min(chunk, out.numel() - i)
+        hi = torch.randint(0, 1 << 32, (m,), dtype=torch.int64, device=out.device, generator=gen)
+        lo = torch.randint(0, 1 << 32, (m,), dtype=torch.int64, device=out.device, generator=gen)
+        out[i:i + m] = (hi << 32) | lo
+
+
+def _mix(torch, k64, v64):
+    """Order-independent fingerprint term of (key, value) pairs: int64 sums wrap."""
+    return ((k64 * -7046029254386353131) ^ (v64 * -4417276706812531889) ^ (k64 >> 29)).sum()
+
+
+def run_mg_extras(torch, dev, lib, L, peak, rank, world, max_over_ranks, barrier, shrink=0, steps=3):
+    """BASELINE config 5 at this N (strong scaling, total work fixed):
+    5a global SortPairs of 2^31 uniform u64 keys + u32 values (= global index),
+    5b ExclusiveSum of 2^32 u32 values uniform in [0,16), both sharded evenly
+    in rank order and run through the multi-GPU C ABI (lcpp_mg_sort,
+    lcpp_mg_scan).  Per-phase device times come from the library's events;
+    the untimed checks verify the global result on the device."""
+    from lc_parallel_primitive_b200 import multi_gpu as M
+
+    comm = M.comm_for() if world > 1 else None
+    stream = torch.cuda.current_stream()
+    out = {}
+    gen = torch.Generator(device=dev)
+
+    def phases(names):
+        res = {}
+        for nm in names:
+            c, t = L.C.c_uint64(0), L.C.c_double(0)
+            lib.lcpp_profile_read(nm.encode(), L.C.byref(c), L.C.byref(t))
+            res[nm + "_ms"] = max_over_ranks(float(t.value) / max(int(c.value), 1))
+        return res
+
+    def timed(fn, k):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(k):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(a.elapsed_time(b) / k)
+
+    if comm is None:  # one rank: a 1-rank communicator through the same C ABI
+        import ctypes as C
+
+        uid = C.create_string_buffer(int(lib.lcpp_mg_unique_id_bytes()))
+        L.check(lib.lcpp_mg_get_unique_id(uid))
+        h = C.c_void_p()
+        L.check(lib.lcpp_mg_comm_init_rank(C.byref(h), 1, uid, 0))
+
+        class _One:
+            handle, world, nranks, rank = h, 1, 1, 0
+        comm = _One()
+    nr = L.C.c_int(0)
+    L.check(lib.lcpp_mg_comm_shape(comm.handle, L.C.byref(L.C.c_int(0)), L.C.byref(nr)))
+
+    # ---- 5a ------------------------------------------------------------------
+    N = 1 << (31 - shrink)
+    n = N // world
+    gen.manual_seed(1000 + rank)
+    keys = torch.empty(n, dtype=torch.int64, device=dev)
+    _fill_u64_uniform(torch, keys, gen)
+    vals = torch.arange(rank * n, rank * n + n, dtype=torch.int64, device=dev).to(torch.int32)
+    cap = M.default_capacity(n) if world > 1 else n
+    ko = torch.empty(cap, dtype=torch.int64, device=dev)
+    vo = torch.empty(cap, dtype=torch.int32, device=dev)
+    tb = M.mg_sort_temp_bytes(keys.view(torch.uint64), vals.view(torch.uint32), cap, world)
+    temp = torch.empty(tb, dtype=torch.uint8, device=dev)
+    res = {}
+
+    def sort5a():
+        res["r"] = M.mg_sort_pairs(keys.view(torch.uint64), vals.view(torch.uint32), comm=comm, capacity=cap,
+                                   temp=temp, keys_out=ko.view(torch.uint64), vals_out=vo.view(torch.uint32))
+
+    sort5a()
+    torch.cuda.synchronize()
+    L.check(lib.lcpp_last_device_error(stream.cuda_stream), "device error (5a)")
+    # untimed global check: order, continuity across ranks, count, stability, pairs kept together
+    m = res["r"].n
+    sk = ko[:m] ^ (-(1 << 63))  # unsigned order as signed
+    sv = vo[:m].to(torch.int64) & 0xFFFFFFFF
+    ok = bool((sk[1:] >= sk[:-1]).all()) if m > 1 else True
+    eq = sk[1:] == sk[:-1]
+    ok &= bool((sv[1:][eq] > sv[:-1][eq]).all()) if m > 1 else True
+    fp_in = _mix(torch, keys, vals.to(torch.int64) & 0xFFFFFFFF)
+    fp_out = _mix(torch, ko[:m], sv)
+    stats = torch.tensor([m, 0, 0], dtype=torch.int64, device=dev)
+    stats[1] = fp_in
+    stats[2] = fp_out
+    ends = torch.tensor([sk[0].item() if m else 0, sk[-1].item() if m else 0, sv[0].item() if m else 0,
+                         sv[-1].item() if m else 0, m], dtype=torch.int64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(stats)
+        allends = [torch.empty_like(ends) for _ in range(world)]
+        torch.distributed.all_gather(allends, ends)
+        e = [t.cpu().tolist() for t in allends]
+        e = [x for x in e if x[4] > 0]
+        for a_, b_ in zip(e, e[1:]):
+            ok &= a_[1] < b_[0] or (a_[1] == b_[0] and a_[3] < b_[2])
+    st = stats.cpu().tolist()
+    ok &= st[0] == N and st[1] == st[2]
+    del sk, sv, eq
+    lib.lcpp_profile_enable(1)
+    ms = timed(sort5a, steps)
+    ph = phases(["mg_splitters", "mg_partition", "mg_plan", "mg_exchange", "mg_local_sort", "rs_onesweep"])
+    lib.lcpp_profile_enable(0)
+    per_pair = 200 if world == 1 else 268  # modelled HBM bytes per local pair (DESIGN: 5a)
+    out[f"mg_sort_pairs_u64_2p{31 - shrink}"] = {
+        "ms": ms, "Gpairs/s": N / (ms * 1e-3) / 1e9, "n_gpus": world, "n_per_gpu": n, "scaling": "strong",
+        "check_ok": bool(ok), "max_slice": int(max_over_ranks(float(m))), "comm_nranks": nr.value,
+        "hbm_bytes_per_pair_model": per_pair,
+        "hbm_frac_model": per_pair * n / (ms * 1e-3) / 1e9 / peak,
+        "nvlink_bytes_per_gpu": 12 * n * (world - 1) // world, **ph}
+    del keys, vals, ko, vo, temp, res
+    torch.cuda.empty_cache()
+
+    # ---- 5b ------------------------------------------------------------------
+    N = 1 << (32 - shrink)
+    n = N // world
+    gen.manual_seed(2000 + rank)
+    x = torch.empty(n, dtype=torch.int32, device=dev)
+    chunk = 1 << 27
+    for i in range(0, n, chunk):
+        x[i:i + chunk] = torch.randint(0, 16, (min(chunk, n - i),), dtype=torch.int32, device=dev, generator=gen)
+    y = torch.empty_like(x)
+    tb = M.mg_scan_temp_bytes(x.view(torch.uint32), world)
+    temp = torch.empty(tb, dtype=torch.uint8, device=dev)
+
+    def scan5b():
+        M.mg_scan(False, x.view(torch.uint32), y.view(torch.uint32), comm=comm, temp=temp)
+
+    scan5b()
+    torch.cuda.synchronize()
+    L.check(lib.lcpp_last_device_error(stream.cuda_stream), "device error (5b)")
+    ok = True
+    for i in range(0, n - 1, chunk):  # out[i+1] - out[i] == x[i] (mod 2^32), in chunks
+        j = min(i + chunk, n - 1)
+        ok &= bool(((y[i + 1:j + 1] - y[i:j]) == x[i:j]).all())
+    first = int(y[0].item())
+    tail = torch.tensor([int(y[-1].item()) + int(x[-1].item()), first], dtype=torch.int64, device=dev)
+    if world > 1:
+        allt = [torch.empty_like(tail) for _ in range(world)]
+        torch.distributed.all_gather(allt, tail)
+        t = [a_.cpu().tolist() for a_ in allt]
+        ok &= t[0][1] == 0 and all((t[r][0] & 0xFFFFFFFF) == (t[r + 1][1] & 0xFFFFFFFF) for r in range(world - 1))
+    else:
+        ok &= first == 0
+    lib.lcpp_profile_enable(1)
+    ms = timed(scan5b, max(steps, 5))
+    ph = phases(["mg_local_reduce", "mg_allgather", "mg_carry_scan"])
+    lib.lcpp_profile_enable(0)
+    out[f"mg_exclusive_sum_u32_2p{32 - shrink}"] = {
+        "ms": ms, "GB/s_per_gpu_8B": 8 * n / (ms * 1e-3) / 1e9, "frac_8B": 8 * n / (ms * 1e-3) / 1e9 / peak,
+        "frac_12B_structural": 12 * n / (ms * 1e-3) / 1e9 / peak, "n_gpus": world, "n_per_gpu": n,
+        "scaling": "strong", "check_ok": bool(ok), "comm_nranks": nr.value, **ph}
+    del x, y, temp
+    torch.cuda.empty_cache()
+    if world == 1:
+        L.check(lib.lcpp_mg_comm_destroy(comm.handle))
     return out
 
 
