@@ -676,20 +676,33 @@ def run_mg_extras(torch, dev, lib, L, peak, rank, world, max_over_ranks, barrier
     sort5a()
     torch.cuda.synchronize()
     L.check(lib.lcpp_last_device_error(stream.cuda_stream), "device error (5a)")
-    # untimed global check: order, continuity across ranks, count, stability, pairs kept together
+    # untimed global check: order, continuity across ranks, count, stability,
+    # pairs kept together (fingerprint of (key, value) before and after); in
+    # chunks, so that the check needs little memory beside the buffers
     m = res["r"].n
-    sk = ko[:m] ^ (-(1 << 63))  # unsigned order as signed
-    sv = vo[:m].to(torch.int64) & 0xFFFFFFFF
-    ok = bool((sk[1:] >= sk[:-1]).all()) if m > 1 else True
-    eq = sk[1:] == sk[:-1]
-    ok &= bool((sv[1:][eq] > sv[:-1][eq]).all()) if m > 1 else True
-    fp_in = _mix(torch, keys, vals.to(torch.int64) & 0xFFFFFFFF)
-    fp_out = _mix(torch, ko[:m], sv)
-    stats = torch.tensor([m, 0, 0], dtype=torch.int64, device=dev)
-    stats[1] = fp_in
-    stats[2] = fp_out
-    ends = torch.tensor([sk[0].item() if m else 0, sk[-1].item() if m else 0, sv[0].item() if m else 0,
-                         sv[-1].item() if m else 0, m], dtype=torch.int64, device=dev)
+    ok = True
+    fp_in = torch.zeros((), dtype=torch.int64, device=dev)
+    fp_out = torch.zeros((), dtype=torch.int64, device=dev)
+    chunk = 1 << 26
+    for i in range(0, n, chunk):
+        j = min(i + chunk, n)
+        fp_in += _mix(torch, keys[i:j], vals[i:j].to(torch.int64) & 0xFFFFFFFF)
+    for i in range(0, m, chunk):
+        j = min(i + chunk + 1, m)  # one item of overlap with the next chunk
+        sk = ko[i:j] ^ (-(1 << 63))  # unsigned order as signed
+        sv = vo[i:j].to(torch.int64) & 0xFFFFFFFF
+        if j - i > 1:
+            ok &= bool((sk[1:] >= sk[:-1]).all())
+            eq = sk[1:] == sk[:-1]
+            ok &= bool((sv[1:][eq] > sv[:-1][eq]).all())
+        k_ = min(i + chunk, m)
+        fp_out += _mix(torch, ko[i:k_], vo[i:k_].to(torch.int64) & 0xFFFFFFFF)
+        del sk, sv
+    stats = torch.stack([torch.tensor(m, dtype=torch.int64, device=dev), fp_in, fp_out])
+    first = (ko[0] ^ (-(1 << 63))).item() if m else 0
+    last = (ko[m - 1] ^ (-(1 << 63))).item() if m else 0
+    ends = torch.tensor([first, last, int(vo[0].item()) & 0xFFFFFFFF if m else 0,
+                         int(vo[m - 1].item()) & 0xFFFFFFFF if m else 0, m], dtype=torch.int64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(stats)
         allends = [torch.empty_like(ends) for _ in range(world)]
@@ -700,7 +713,6 @@ def run_mg_extras(torch, dev, lib, L, peak, rank, world, max_over_ranks, barrier
             ok &= a_[1] < b_[0] or (a_[1] == b_[0] and a_[3] < b_[2])
     st = stats.cpu().tolist()
     ok &= st[0] == N and st[1] == st[2]
-    del sk, sv, eq
     lib.lcpp_profile_enable(1)
     ms = timed(sort5a, steps)
     ph = phases(["mg_splitters", "mg_partition", "mg_plan", "mg_exchange", "mg_local_sort", "rs_onesweep"])

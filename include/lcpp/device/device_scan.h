@@ -2,9 +2,8 @@
  * DeviceScan — same class template, methods and argument meaning as the
  * reference (src/lcpp/device/device_scan.h:33-345); single-pass decoupled
  * look-back scans in liblcpp_b200.so through lcpp_scan*() and
- * lcpp_scan_by_key().  Element types of the plain scans: the reference's
- * Type4Byte (int32, uint32, float); ScanByKey takes any of the six numeric
- * types for keys and values.
+ * lcpp_scan_by_key().  Element types: any of the six numeric types (int32,
+ * uint32, float, int64, uint64, double), as the reference's NumericT.
  */
 #pragma once
 #include "lcpp/runtime/core.h"
@@ -95,7 +94,6 @@ class DeviceScan : public LuisaModule {
     template <typename T>
     void record_op(CommandList& cmdlist, int kind, int op, BufferView<uint> temp, BufferView<T> in,
                    BufferView<T> out, size_t n, T init) {
-        static_assert(sizeof(T) == 4, "DeviceScan serves 4-byte types");
         cmdlist << [=](cudaStream_t s) {
             return lcpp_scan_op(kind, op, lcpp_dtype_of<T>(), in.data(), out.data(), n, &init, temp.data(),
                                 temp.size_bytes(), s);
@@ -105,7 +103,6 @@ class DeviceScan : public LuisaModule {
     template <typename T>
     void record(CommandList& cmdlist, int kind, BufferView<uint> temp, BufferView<T> in, BufferView<T> out,
                 size_t n) {
-        static_assert(sizeof(T) == 4, "DeviceScan serves 4-byte types");
         cmdlist << [=](cudaStream_t s) {
             return lcpp_scan(kind, lcpp_dtype_of<T>(), in.data(), out.data(), n, temp.data(), temp.size_bytes(), s);
         };

@@ -83,7 +83,8 @@ lcpp_status lcpp_reduce(int op, int dtype, const void* in, void* out, uint64_t n
  * Exclusive: out[i] = sum(in[0..i)), out[0] = 0.  Inclusive: sum(in[0..i]).
  * Replaces DeviceScan::ExclusiveSum/InclusiveSum (device_scan.h:180-204) and
  * GetTempStorageBytes (device_scan.h:75-89).  Single-pass decoupled
- * look-back.  dtype: I32 U32 F32 (the reference's Type4Byte).  In-place
+ * look-back.  dtype: any of I32 U32 F32 I64 U64 F64 (the reference's
+ * NumericT, common/type_trait.h:11-14); integer sums wrap.  In-place
  * (in == out) is allowed. */
 size_t      lcpp_scan_temp_bytes(int dtype, uint64_t n);
 lcpp_status lcpp_scan(int kind, int dtype, const void* in, void* out, uint64_t n,
@@ -137,11 +138,14 @@ lcpp_status lcpp_radix_bucket_starts(int key_dtype, const void* keys, uint64_t n
  * (device_segment_reduce.h:125-194; Max's init is lowest(), :186-194).
  * dtype: any of I32 U32 F32 I64 U64 F64.  Offsets are uint32 (the
  * reference's BufferView<uint>); a CSR offsets[S+1] array is passed as
- * begin = offsets, end = offsets + 1.  temp may be NULL or smaller than
- * lcpp_segment_reduce_temp_bytes(): the call then reduces every segment with
- * one warp (the reference's GetTempStorageBytes returns 0 here,
- * device_segment_reduce.h:71-75); with the full temp, segments longer than
- * 4096 items go to whole CTAs. */
+ * begin = offsets, end = offsets + 1.  With the temp of
+ * lcpp_segment_reduce_temp_bytes(dtype, num_items, S) (num_items = the last
+ * end offset) and monotone offsets (begin[s] <= end[s] <= begin[s+1], e.g.
+ * CSR), the work is split by items into 32 KiB tiles, whatever the segment
+ * lengths; other offsets are reduced one warp per segment (checked on the
+ * device).  temp may be NULL or smaller (the reference's GetTempStorageBytes
+ * returns 0 here, device_segment_reduce.h:71-75): the call then reduces one
+ * warp per segment. */
 size_t      lcpp_segment_reduce_temp_bytes(int dtype, uint64_t num_items,
                                            uint64_t num_segments);
 lcpp_status lcpp_segment_reduce(int op, int dtype, const void* in, void* out,
@@ -255,7 +259,7 @@ lcpp_status lcpp_mg_reduce(int op, int dtype, const void* in, void* out, uint64_
 /* Prefix sum of the global sequence; each rank writes its shard's part.
  * Local reduce -> all-gather of the G shard totals -> carry = sum of the
  * lower ranks' totals (rank order) -> local scan seeded with the carry.
- * Integer results are bit-exact (mod 2^bits).  dtype: I32 U32 F32.
+ * Integer results are bit-exact (mod 2^bits).  dtype: any of the six.
  * Asynchronous. */
 size_t      lcpp_mg_scan_temp_bytes(int dtype, uint64_t n_local, int nranks);
 lcpp_status lcpp_mg_scan(int kind, int dtype, const void* in, void* out, uint64_t n_local,

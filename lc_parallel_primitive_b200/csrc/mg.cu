@@ -433,6 +433,11 @@ extern "C" lcpp_status lcpp_mg_scan(int kind, int dtype, const void* in, void* o
     char* rtemp = base + head;
     char* stemp = rtemp + rt;
     lcpp_status st;
+    if (G == 1) {  // no carry to exchange: the local scan is the global scan
+        ProfScope ps("mg_carry_scan", s);
+        return n_local ? lcpp_scan_carry(kind, dtype, in, out, n_local, nullptr, stemp, temp_bytes - head - rt, stream)
+                       : LCPP_OK;
+    }
     {
         ProfScope ps("mg_local_reduce", s);
         st = lcpp_reduce(LCPP_OP_SUM, dtype, in, total, n_local, rtemp, rt, stream);

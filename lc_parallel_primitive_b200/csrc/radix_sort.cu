@@ -225,12 +225,6 @@ constexpr size_t rs_smem_bytes() {
            (size_t)(THREADS / 32) * RS_DIGITS * 4 * 2 + RS_DIGITS * 4 * 2 + 64;
 }
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 template <typename KB, typename VB, typename W, int KIND, bool DESC, int THREADS, bool DIG = false>
 __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(RsPass a) {

@@ -25,15 +25,20 @@ namespace lcpp {
 constexpr int SCAN_THREADS = 1024;
 constexpr int SCAN_WARPS = SCAN_THREADS / 32;
 constexpr int SCAN_VECS = 8;                       // 16-byte vectors per thread
-constexpr int SCAN_ITEMS = SCAN_VECS * 4;          // 32 items (4-byte types)
-constexpr int SCAN_WARP_ITEMS = 32 * SCAN_ITEMS;   // 1024
-constexpr int SCAN_TILE = SCAN_THREADS * SCAN_ITEMS;  // 32768
 constexpr size_t SCAN_HDR = 256;                   // ticket counter + padding
-constexpr int SCAN_DESC_TILE = 8192;               // smallest tile of any scan kernel: sizes the descriptors
+// Items per 16-byte vector and per tile of scan_kernel (32768 4-byte or
+// 16384 8-byte items).
+template <typename T> __host__ __device__ constexpr int scan_vec_items() { return 16 / (int)sizeof(T); }
+template <typename T> __host__ __device__ constexpr int scan_tile_items() { return SCAN_THREADS * SCAN_VECS * scan_vec_items<T>(); }
+constexpr int SCAN_TILE = SCAN_THREADS * SCAN_VECS * 4;  // 4-byte types
+// Smallest tile of any scan kernel (the pipelined kernel's 32 KiB tiles)
+// sizes the descriptor arrays: 8192 4-byte or 4096 8-byte items.
+constexpr int SCAN_DESC_TILE_BYTES = 32768;
+constexpr int SCAN_DESC_TILE = SCAN_DESC_TILE_BYTES / 4;
 
 template <typename Op, typename T>
 static lcpp_status scan_pipe_launch(bool inclusive, const T* in, T* out, uint64_t n, const T* carry_in, T init,
-                                    unsigned int* ticket, uint64_t* desc, cudaStream_t s);
+                                    unsigned int* ticket, void* desc, cudaStream_t s);
 
 constexpr uint64_t ST_PARTIAL = 1ull << 32;
 constexpr uint64_t ST_INCLUSIVE = 2ull << 32;
@@ -45,6 +50,66 @@ template <typename T> __device__ __forceinline__ T from_bits(uint32_t b) { retur
 template <> __device__ __forceinline__ uint32_t from_bits<uint32_t>(uint32_t b) { return b; }
 template <> __device__ __forceinline__ int32_t from_bits<int32_t>(uint32_t b) { return (int32_t)b; }
 
+// Tile descriptors of the look-back.  status: 0 not yet published,
+// 1 partial (tile aggregate), 2 inclusive (prefix through the tile).
+//  * 4-byte values: one 64-bit word {status:32 | value:32} per tile, written
+//    and read with relaxed device-scope accesses, so value and status are
+//    always seen together (the reference writes them as separate volatile
+//    stores with no fence, single_pass_scan_operator.h:81-93).
+//  * 8-byte values: a status word per tile plus an aggregate slot and an
+//    inclusive slot; the value is stored before a release store of the
+//    status, and read after an acquire load of it.
+template <typename T, bool WIDE = (sizeof(T) == 8)>
+struct ScanDesc;
+
+template <typename T>
+struct ScanDesc<T, false> {
+    uint64_t* w;
+    static size_t bytes(uint64_t tiles) { return align_up(tiles * sizeof(uint64_t), 256); }
+    static ScanDesc carve(void* p, uint64_t) { return ScanDesc{(uint64_t*)p}; }
+    __device__ __forceinline__ void partial(int64_t t, T v) const { st_relaxed_u64(w + t, ST_PARTIAL | to_bits<T>(v)); }
+    __device__ __forceinline__ void inclusive(int64_t t, T v) const { st_relaxed_u64(w + t, ST_INCLUSIVE | to_bits<T>(v)); }
+    __device__ __forceinline__ uint32_t load(int64_t t, T& v) const {
+        const uint64_t d = ld_relaxed_u64(w + t);
+        v = from_bits<T>((uint32_t)d);
+        return (uint32_t)(d >> 32);
+    }
+};
+
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <typename T>
+struct ScanDesc<T, true> {
+    uint32_t* status;
+    T* agg;
+    T* incl;
+    static size_t bytes(uint64_t tiles) { return align_up(tiles * 4, 256) + 2 * align_up(tiles * 8, 256); }
+    static ScanDesc carve(void* p, uint64_t tiles) {
+        char* c = (char*)p;
+        return ScanDesc{(uint32_t*)c, (T*)(c + align_up(tiles * 4, 256)),
+                        (T*)(c + align_up(tiles * 4, 256) + align_up(tiles * 8, 256))};
+    }
+    __device__ __forceinline__ void partial(int64_t t, T v) const {
+        st_relaxed_u64(reinterpret_cast<uint64_t*>(agg + t), __builtin_bit_cast(uint64_t, v));
+        st_release_u32(status + t, 1u);
+    }
+    __device__ __forceinline__ void inclusive(int64_t t, T v) const {
+        st_relaxed_u64(reinterpret_cast<uint64_t*>(incl + t), __builtin_bit_cast(uint64_t, v));
+        st_release_u32(status + t, 2u);
+    }
+    __device__ __forceinline__ uint32_t load(int64_t t, T& v) const {
+        const uint32_t st = ld_acquire_u32(status + t);
+        if (st) v = __builtin_bit_cast(T, ld_relaxed_u64(reinterpret_cast<const uint64_t*>(st == 1 ? agg + t : incl + t)));
+        return st;
+    }
+};
 
 __device__ __forceinline__ void backoff(uint32_t it) {
     if (it > 64) __nanosleep(it < 1024 ? 32 : 128);
@@ -54,25 +119,25 @@ __device__ __forceinline__ void backoff(uint32_t it) {
 // aggregates of all preceding tiles (same value in every lane).  Lane L
 // inspects tile (window_end - L); windows of 32 move towards tile 0 until an
 // inclusive descriptor is found.
-template <typename Op, typename T>
-__device__ T lookback_warp(const uint64_t* desc, int64_t tile) {
+template <typename Op, typename T, typename D>
+__device__ T lookback_warp(const D& desc, int64_t tile) {
     const int lane = threadIdx.x & 31;
     const uint32_t limit = g_spin_limit;
     T acc = Op::template identity<T>();
     int64_t p = tile - 1 - lane;
     uint32_t spins = 0;
     while (true) {
-        uint64_t d = p >= 0 ? ld_relaxed_u64(desc + p) : (ST_INCLUSIVE | to_bits<T>(Op::template identity<T>()));
-        while (__any_sync(0xffffffffu, (d >> 32) == 0)) {
+        T v = Op::template identity<T>();
+        uint32_t st = p >= 0 ? desc.load(p, v) : 2u;
+        while (__any_sync(0xffffffffu, st == 0)) {
             if (++spins > limit) {
                 if (lane == 0) set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
                 return warp_reduce<Op>(acc);
             }
             backoff(spins);
-            if ((d >> 32) == 0) d = ld_relaxed_u64(desc + p);
+            if (st == 0) st = desc.load(p, v);
         }
-        const uint32_t incl = __ballot_sync(0xffffffffu, (d >> 32) == 2);
-        T v = from_bits<T>((uint32_t)d);
+        const uint32_t incl = __ballot_sync(0xffffffffu, st == 2);
         if (incl) {
             const int first = __ffs(incl) - 1;
             if (lane > first) v = Op::template identity<T>();
@@ -85,23 +150,26 @@ __device__ T lookback_warp(const uint64_t* desc, int64_t tile) {
 
 // Warp 0 of a tile: publish the tile aggregate, resolve the exclusive prefix,
 // publish the inclusive value.  Returns the exclusive prefix in every lane.
-template <typename Op, typename T>
-__device__ __forceinline__ T tile_prefix(uint64_t* desc, int64_t tile, T aggregate, T carry) {
+template <typename Op, typename T, typename D>
+__device__ __forceinline__ T tile_prefix(const D& desc, int64_t tile, T aggregate, T carry) {
     const int lane = threadIdx.x & 31;
     if (tile == 0) {
-        if (lane == 0) st_relaxed_u64(desc, ST_INCLUSIVE | to_bits<T>(Op::template apply<T>(carry, aggregate)));
+        if (lane == 0) desc.inclusive(0, Op::template apply<T>(carry, aggregate));
         return carry;
     }
-    if (lane == 0) st_relaxed_u64(desc + tile, ST_PARTIAL | to_bits<T>(aggregate));
+    if (lane == 0) desc.partial(tile, aggregate);
     const T excl = lookback_warp<Op, T>(desc, tile);
-    if (lane == 0) st_relaxed_u64(desc + tile, ST_INCLUSIVE | to_bits<T>(Op::template apply<T>(excl, aggregate)));
+    if (lane == 0) desc.inclusive(tile, Op::template apply<T>(excl, aggregate));
     return excl;
 }
 
-template <typename Op, typename T, bool INCLUSIVE>
+template <typename Op, typename T, bool INCLUSIVE, typename D = ScanDesc<T>>
 __global__ void __launch_bounds__(SCAN_THREADS, 1)
 scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in, T init,
-            unsigned int* ticket, uint64_t* desc) {
+            unsigned int* ticket, D desc) {
+    constexpr int V = scan_vec_items<T>();
+    constexpr int WARP_ITEMS = 32 * SCAN_VECS * V;
+    constexpr int TILE = scan_tile_items<T>();
     __shared__ unsigned int s_tile;
     __shared__ T s_warp[SCAN_WARPS];
 
@@ -109,26 +177,26 @@ scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in, T init,
     if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1u);
     __syncthreads();
     const int64_t tile = s_tile;
-    const uint64_t tile_base = (uint64_t)tile * SCAN_TILE;
-    const uint64_t base = tile_base + (uint64_t)warp * SCAN_WARP_ITEMS + lane * 4;
-    const bool vec_ok = tile_base + SCAN_TILE <= n &&
+    const uint64_t tile_base = (uint64_t)tile * TILE;
+    const uint64_t base = tile_base + (uint64_t)warp * WARP_ITEMS + lane * V;
+    const bool vec_ok = tile_base + TILE <= n &&
                         ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
 
-    T x[SCAN_VECS][4];
+    T x[SCAN_VECS][V];
     if (vec_ok) {
 #pragma unroll
         for (int j = 0; j < SCAN_VECS; ++j) {
-            const uint4 q = ld_stream(reinterpret_cast<const uint4*>(in + base + j * 128));
+            const uint4 q = ld_stream(reinterpret_cast<const uint4*>(in + base + j * 32 * V));
             const T* e = reinterpret_cast<const T*>(&q);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) x[j][k] = e[k];
+            for (int k = 0; k < V; ++k) x[j][k] = e[k];
         }
     } else {
 #pragma unroll
         for (int j = 0; j < SCAN_VECS; ++j)
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint64_t i = base + j * 128 + k;
+            for (int k = 0; k < V; ++k) {
+                const uint64_t i = base + j * 32 * V + k;
                 x[j][k] = i < n ? in[i] : Op::template identity<T>();
             }
     }
@@ -139,8 +207,8 @@ scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in, T init,
 #pragma unroll
     for (int j = 0; j < SCAN_VECS; ++j) {
 #pragma unroll
-        for (int k = 1; k < 4; ++k) x[j][k] = Op::template apply<T>(x[j][k - 1], x[j][k]);
-        T incl = x[j][3];
+        for (int k = 1; k < V; ++k) x[j][k] = Op::template apply<T>(x[j][k - 1], x[j][k]);
+        T incl = x[j][V - 1];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const T y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -166,7 +234,7 @@ scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in, T init,
         const T c0 = carry_in ? *carry_in : init;
         const T block_excl = tile_prefix<Op, T>(desc, tile, aggregate, c0);
         __syncwarp();
-        // All 32 lanes take part in the shuffle; only 16 store.
+        // All 32 lanes take part in the shuffle; only SCAN_WARPS store.
         T wex = __shfl_up_sync(0xffffffffu, incl, 1);
         if (lane == 0) wex = Op::template identity<T>();
         if (lane < SCAN_WARPS) s_warp[lane] = Op::template apply<T>(block_excl, wex);
@@ -178,24 +246,24 @@ scan_kernel(const T* in, T* out, uint64_t n, const T* carry_in, T init,
 #pragma unroll
         for (int j = 0; j < SCAN_VECS; ++j) {
             const T b = Op::template apply<T>(wbase, pre[j]);
-            T r[4];
+            T r[V];
             if (INCLUSIVE) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) r[k] = Op::template apply<T>(b, x[j][k]);
+                for (int k = 0; k < V; ++k) r[k] = Op::template apply<T>(b, x[j][k]);
             } else {
                 r[0] = b;
 #pragma unroll
-                for (int k = 1; k < 4; ++k) r[k] = Op::template apply<T>(b, x[j][k - 1]);
+                for (int k = 1; k < V; ++k) r[k] = Op::template apply<T>(b, x[j][k - 1]);
             }
-            __stcs(reinterpret_cast<uint4*>(out + base + j * 128), *reinterpret_cast<const uint4*>(r));
+            __stcs(reinterpret_cast<uint4*>(out + base + j * 32 * V), *reinterpret_cast<const uint4*>(r));
         }
     } else {
 #pragma unroll
         for (int j = 0; j < SCAN_VECS; ++j) {
             const T b = Op::template apply<T>(wbase, pre[j]);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint64_t i = base + j * 128 + k;
+            for (int k = 0; k < V; ++k) {
+                const uint64_t i = base + j * 32 * V + k;
                 if (i < n) out[i] = INCLUSIVE ? Op::template apply<T>(b, x[j][k]) : (k ? Op::template apply<T>(b, x[j][k - 1]) : b);
             }
         }
@@ -210,7 +278,7 @@ __global__ void lookback_tiles_kernel(const uint32_t* agg, uint32_t* excl_out, u
     __syncwarp();
     const int64_t tile = s_tile;
     const uint32_t a = agg[tile];
-    const uint32_t e = tile_prefix<OpSum, uint32_t>(desc, tile, a, 0u);
+    const uint32_t e = tile_prefix<OpSum, uint32_t>(ScanDesc<uint32_t>{desc}, tile, a, 0u);
     if (threadIdx.x == 0) {
         excl_out[tile] = e;
         incl_out[tile] = e + a;
@@ -218,7 +286,7 @@ __global__ void lookback_tiles_kernel(const uint32_t* agg, uint32_t* excl_out, u
 }
 
 __global__ void lookback_probe_kernel(const uint64_t* desc, int64_t tile, uint32_t* excl_out) {
-    const uint32_t e = lookback_warp<OpSum, uint32_t>(desc, tile);
+    const uint32_t e = lookback_warp<OpSum, uint32_t>(ScanDesc<uint32_t>{const_cast<uint64_t*>(desc)}, tile);
     if (threadIdx.x == 0) *excl_out = e;
 }
 
@@ -226,10 +294,13 @@ __global__ void lookback_probe_kernel(const uint64_t* desc, int64_t tile, uint32
 
 using namespace lcpp;
 
+static size_t scan_desc_tiles(size_t es, uint64_t n) { return ceil_div(n ? n : 1, SCAN_DESC_TILE_BYTES / es); }
+
 extern "C" size_t lcpp_scan_temp_bytes(int dtype, uint64_t n) {
-    if (dtype != LCPP_I32 && dtype != LCPP_U32 && dtype != LCPP_F32) return 0;
-    const uint64_t tiles = ceil_div(n ? n : 1, SCAN_DESC_TILE);
-    return SCAN_HDR + align_up(tiles * sizeof(uint64_t), 256);
+    const size_t es = lcpp_dtype_size(dtype);
+    if (!es || dtype == LCPP_NONE) return 0;
+    const uint64_t tiles = scan_desc_tiles(es, n);
+    return SCAN_HDR + (es == 4 ? ScanDesc<uint32_t>::bytes(tiles) : ScanDesc<uint64_t>::bytes(tiles));
 }
 
 // Shared body of the scan entry points: op in {SUM, MIN, MAX}; the device
@@ -242,24 +313,28 @@ static lcpp_status scan_impl(int kind, int op, int dtype, const void* in, void* 
     if (!need) return LCPP_ERR_INVALID_ARG;
     if (n == 0) return LCPP_OK;
     if (!temp || temp_bytes < need) return LCPP_ERR_TEMP_TOO_SMALL;
-    const uint64_t tiles = ceil_div(n, SCAN_TILE);
-    const uint64_t desc_tiles = ceil_div(n, SCAN_DESC_TILE);
+    const size_t es = lcpp_dtype_size(dtype);
+    const uint64_t desc_tiles = scan_desc_tiles(es, n);
     if (desc_tiles > 0xffffffffull) return LCPP_ERR_INVALID_ARG;
     const bool aligned = ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
     cudaStream_t s = (cudaStream_t)stream;
     unsigned int* ticket = (unsigned int*)temp;
-    uint64_t* desc = (uint64_t*)((char*)temp + SCAN_HDR);
-    if (cudaMemsetAsync(temp, 0, SCAN_HDR + (aligned ? desc_tiles : tiles) * sizeof(uint64_t), s) != cudaSuccess)
-        return LCPP_ERR_CUDA;
+    void* desc_mem = (char*)temp + SCAN_HDR;
     auto go_op = [&](auto zero, auto opv) -> lcpp_status {
         using T = decltype(zero);
         using Op = decltype(opv);
+        using D = ScanDesc<T>;
+        const uint64_t tiles = aligned ? desc_tiles : ceil_div(n, scan_tile_items<T>());
+        // zero the ticket and the descriptors (for 8-byte values the status words)
+        const size_t zero_bytes = SCAN_HDR + (sizeof(T) == 4 ? tiles * 8 : tiles * 4);
+        if (cudaMemsetAsync(temp, 0, zero_bytes, s) != cudaSuccess) return LCPP_ERR_CUDA;
+        const D desc = D::carve(desc_mem, desc_tiles);
         const T iv = init ? *(const T*)init : Op::template identity<T>();
         const T* ci = (const T*)carry_in;
         ProfScope ps("scan", s);
         if (aligned)  // pipelined persistent kernel (scan_pipe.cu)
             return scan_pipe_launch<Op, T>(kind == LCPP_SCAN_INCLUSIVE, (const T*)in, (T*)out, n, ci, iv, ticket,
-                                           desc, s);
+                                           desc_mem, s);
         if (kind == LCPP_SCAN_INCLUSIVE)
             scan_kernel<Op, T, true><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, ci, iv, ticket, desc);
         else
@@ -274,11 +349,7 @@ static lcpp_status scan_impl(int kind, int op, int dtype, const void* in, void* 
             default: return go_op(zero, OpMax{});
         }
     };
-    switch (dtype) {
-        case LCPP_I32: return go((int32_t)0);
-        case LCPP_U32: return go((uint32_t)0);
-        default: return go((float)0);
-    }
+    return dispatch_dtype(dtype, go);
 }
 
 extern "C" lcpp_status lcpp_scan_carry(int kind, int dtype, const void* in, void* out, uint64_t n,
@@ -307,7 +378,7 @@ extern "C" lcpp_status lcpp_lookback_tiles(const uint32_t* aggregates, uint32_t*
     if (!aggregates || !exclusive_out || !inclusive_out || num_tiles > 0x7fffffffull) return LCPP_ERR_INVALID_ARG;
     if (!temp || temp_bytes < lcpp_lookback_temp_bytes(num_tiles)) return LCPP_ERR_TEMP_TOO_SMALL;
     cudaStream_t s = (cudaStream_t)stream;
-    if (cudaMemsetAsync(temp, 0, SCAN_HDR + num_tiles * 8, s) != cudaSuccess) return LCPP_ERR_CUDA;
+    if (cudaMemsetAsync(temp, 0, SCAN_HDR + num_tiles * 8, s) != cudaSuccess) return LCPP_ERR_CUDA;  // 64-bit words
     lookback_tiles_kernel<<<(unsigned)num_tiles, 32, 0, s>>>(aggregates, exclusive_out, inclusive_out,
                                                              (unsigned int*)temp,
                                                              (uint64_t*)((char*)temp + SCAN_HDR));

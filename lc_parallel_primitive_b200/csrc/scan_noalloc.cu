@@ -72,9 +72,9 @@ extern "C" lcpp_status lcpp_scan_noalloc(int kind, int dtype, const void* in, vo
     auto go = [&](auto zero) -> lcpp_status {
         using T = decltype(zero);
         if (kind == LCPP_SCAN_INCLUSIVE)
-            scan_kernel<OpSum, T, true><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, nullptr, T(0), ticket, desc);
+            scan_kernel<OpSum, T, true><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, nullptr, T(0), ticket, ScanDesc<T>{desc});
         else
-            scan_kernel<OpSum, T, false><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, nullptr, T(0), ticket, desc);
+            scan_kernel<OpSum, T, false><<<(unsigned)tiles, SCAN_THREADS, 0, s>>>((const T*)in, (T*)out, n, nullptr, T(0), ticket, ScanDesc<T>{desc});
         count_launch();
         return check_launch();
     };

@@ -25,18 +25,19 @@ namespace lcpp {
 constexpr int SP_THREADS = 512;
 constexpr int SP_WARPS = SP_THREADS / 32;
 constexpr int SP_VECS = 4;
-constexpr int SP_WARP_ITEMS = 32 * SP_VECS * 4;  // 512
-constexpr int SP_TILE = SP_THREADS * SP_VECS * 4;  // 8192
-constexpr int SP_STAGE_BYTES = SP_TILE * 4;
+constexpr int SP_STAGE_BYTES = SP_THREADS * SP_VECS * 16;  // 32 KiB: 8192 4-byte or 4096 8-byte items
 constexpr int SP_CTAS_PER_SM = 2;
 constexpr int SP_STAGES = 3;
 constexpr size_t SP_SMEM = SP_STAGES * (size_t)SP_STAGE_BYTES;
-static_assert(SP_TILE == SCAN_DESC_TILE, "descriptor array is sized for SCAN_DESC_TILE");
+static_assert(SP_STAGE_BYTES == SCAN_DESC_TILE_BYTES, "descriptor arrays are sized for SCAN_DESC_TILE_BYTES tiles");
 
 template <typename Op, typename T, bool INCLUSIVE>
 __global__ void __launch_bounds__(SP_THREADS, SP_CTAS_PER_SM)
 scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* carry_in, T init,
-                 unsigned int* ticket, uint64_t* desc) {
+                 unsigned int* ticket, ScanDesc<T> desc) {
+    constexpr int V = scan_vec_items<T>();
+    constexpr int SP_WARP_ITEMS = 32 * SP_VECS * V;
+    constexpr int SP_TILE = SP_THREADS * SP_VECS * V;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t s_bar[SP_STAGES];
     __shared__ unsigned int s_tile[SP_STAGES];
@@ -48,7 +49,7 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
     const uint64_t full_tiles = n / SP_TILE;
     const uint32_t limit = g_spin_limit;
     const T c0 = carry_in ? *carry_in : init;
-    const uint32_t woff = (uint32_t)warp * SP_WARP_ITEMS + lane * 4;
+    const uint32_t woff = (uint32_t)warp * SP_WARP_ITEMS + lane * V;
     uint32_t phase[SP_STAGES] = {};
 
     auto issue = [&](unsigned int t, int st) {  // thread 0
@@ -75,9 +76,12 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
         T s = Op::template identity<T>();
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
-            const uint4 q = *reinterpret_cast<const uint4*>(buf + woff + j * 128);
+            const uint4 q = *reinterpret_cast<const uint4*>(buf + woff + j * 32 * V);
             const T* e = reinterpret_cast<const T*>(&q);
-            s = Op::template apply<T>(s, Op::template apply<T>(Op::template apply<T>(e[0], e[1]), Op::template apply<T>(e[2], e[3])));
+            if constexpr (V == 4)
+                s = Op::template apply<T>(s, Op::template apply<T>(Op::template apply<T>(e[0], e[1]), Op::template apply<T>(e[2], e[3])));
+            else
+                s = Op::template apply<T>(s, Op::template apply<T>(e[0], e[1]));
         }
         s = warp_reduce<Op>(s);
         __syncthreads();  // earlier readers of s_warp are done
@@ -89,9 +93,9 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
             if (lane == 0) {
                 s_agg[st] = a;
                 if (t == 0)
-                    st_relaxed_u64(desc, ST_INCLUSIVE | to_bits<T>(Op::template apply<T>(c0, a)));
+                    desc.inclusive(0, Op::template apply<T>(c0, a));
                 else
-                    st_relaxed_u64(desc + t, ST_PARTIAL | to_bits<T>(a));
+                    desc.partial((int64_t)t, a);
             }
         }
     };
@@ -99,21 +103,21 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
     // Scan tile t held in stage st (its aggregate already published).
     auto scan_tile = [&](uint64_t t, int st) {
         T* buf = reinterpret_cast<T*>(smem + st * SP_STAGE_BYTES);
-        T x[SP_VECS][4];
+        T x[SP_VECS][V];
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
-            const uint4 q = *reinterpret_cast<const uint4*>(buf + woff + j * 128);
+            const uint4 q = *reinterpret_cast<const uint4*>(buf + woff + j * 32 * V);
             const T* e = reinterpret_cast<const T*>(&q);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) x[j][k] = e[k];
+            for (int k = 0; k < V; ++k) x[j][k] = e[k];
         }
         T pre[SP_VECS];
         T carry = Op::template identity<T>();
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
 #pragma unroll
-            for (int k = 1; k < 4; ++k) x[j][k] = Op::template apply<T>(x[j][k - 1], x[j][k]);
-            T incl = x[j][3];
+            for (int k = 1; k < V; ++k) x[j][k] = Op::template apply<T>(x[j][k - 1], x[j][k]);
+            T incl = x[j][V - 1];
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const T y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -139,7 +143,7 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
             T excl = c0;
             if (t != 0) {
                 excl = lookback_warp<Op, T>(desc, (int64_t)t);
-                if (lane == 0) st_relaxed_u64(desc + t, ST_INCLUSIVE | to_bits<T>(Op::template apply<T>(excl, s_agg[st])));
+                if (lane == 0) desc.inclusive((int64_t)t, Op::template apply<T>(excl, s_agg[st]));
             }
             if (lane < SP_WARPS) s_wex[lane] = Op::template apply<T>(excl, wex);
         }
@@ -149,21 +153,21 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
             const T b = Op::template apply<T>(wbase, pre[j]);
-            T r[4];
+            T r[V];
             if (INCLUSIVE) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) r[k] = Op::template apply<T>(b, x[j][k]);
+                for (int k = 0; k < V; ++k) r[k] = Op::template apply<T>(b, x[j][k]);
             } else {
                 r[0] = b;
 #pragma unroll
-                for (int k = 1; k < 4; ++k) r[k] = Op::template apply<T>(b, x[j][k - 1]);
+                for (int k = 1; k < V; ++k) r[k] = Op::template apply<T>(b, x[j][k - 1]);
             }
             if (full) {
-                *reinterpret_cast<uint4*>(buf + woff + j * 128) = *reinterpret_cast<const uint4*>(r);
+                *reinterpret_cast<uint4*>(buf + woff + j * 32 * V) = *reinterpret_cast<const uint4*>(r);
             } else {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const uint64_t g = t * SP_TILE + woff + j * 128 + k;
+                for (int k = 0; k < V; ++k) {
+                    const uint64_t g = t * SP_TILE + woff + j * 32 * V + k;
                     if (g < n) out[g] = r[k];
                 }
             }
@@ -210,7 +214,8 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
 
 template <typename Op, typename T>
 static lcpp_status scan_pipe_launch(bool inclusive, const T* in, T* out, uint64_t n, const T* carry_in, T init,
-                                    unsigned int* ticket, uint64_t* desc, cudaStream_t s) {
+                                    unsigned int* ticket, void* desc, cudaStream_t s) {
+    constexpr uint64_t SP_TILE = SP_STAGE_BYTES / sizeof(T);
     const uint64_t tiles = ceil_div(n, SP_TILE);
     const DeviceInfo di = device_info();
     uint64_t grid = (uint64_t)di.sms * SP_CTAS_PER_SM;
@@ -218,7 +223,8 @@ static lcpp_status scan_pipe_launch(bool inclusive, const T* in, T* out, uint64_
     auto k = inclusive ? scan_pipe_kernel<Op, T, true> : scan_pipe_kernel<Op, T, false>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SP_SMEM) != cudaSuccess)
         return LCPP_ERR_CUDA;
-    k<<<(unsigned)grid, SP_THREADS, SP_SMEM, s>>>(in, out, n, tiles, carry_in, init, ticket, desc);
+    k<<<(unsigned)grid, SP_THREADS, SP_SMEM, s>>>(in, out, n, tiles, carry_in, init, ticket,
+                                                   ScanDesc<T>::carve(desc, tiles));
     count_launch();
     return check_launch();
 }

@@ -7,7 +7,9 @@
 // (details/segment_reduce.h:98-164).  The reference runs one 256-thread CTA
 // per segment; at 2^20 segments of ~128 items most of those threads idle.
 //
-// B200 mapping:
+// B200 mapping (with a temp buffer from lcpp_segment_reduce_temp_bytes the
+// flat item-tiled path below runs; these two kernels serve calls with less
+// temp, fixed-size segments, and offsets that are not monotone):
 //  * Kernel A: one warp per segment (8 segments per 256-thread CTA), lanes
 //    read consecutive elements (4 independent loads in flight per lane).  A
 //    segment longer than SEG_LONG is not reduced here: its id is appended to a
@@ -120,6 +122,212 @@ seg_block_kernel(const T* __restrict__ in, T* __restrict__ out,
     }
 }
 
+// ---------------------------------------------------------------------------
+// Flat item-tiled path (offsets that are monotone: begin[s] <= end[s] <=
+// begin[s+1]; CSR offsets are).  The work is split by ITEMS, not segments,
+// so every load is an independent 16-byte copy and HBM stays busy whatever
+// the segment lengths:
+//  * segf_partition_kernel (one thread per segment): first segment of every
+//    SEGF_BYTES tile (the first whose end is past the tile start), the tile
+//    count, and a flag if the offsets are not monotone or the tiles do not fit
+//    the temp buffer;
+//  * segf_main_kernel (persistent): a tile's items land in shared memory by
+//    cp.async, then one warp per segment piece reduces it (lane-strided, then
+//    a shuffle tree).  A segment wholly inside the tile is written at once; a
+//    segment that crosses the tile's right edge leaves its piece in carry[c];
+//    one that enters from the left leaves it in head[c];
+//  * segf_fixup_kernel (one warp per tile with a head piece): out[s] = init
+//    (+) carries of the tiles the segment crosses (lane-strided, shuffle tree)
+//    (+) head piece.  Every combination order is fixed, so float results do
+//    not depend on scheduling;
+//  * segf_fallback_kernel: when the flag is set, one warp per segment as
+//    above; otherwise it returns at once.
+// ---------------------------------------------------------------------------
+constexpr int SEGF_THREADS = 256;
+constexpr int SEGF_WARPS = SEGF_THREADS / 32;
+constexpr int SEGF_BYTES = 32768;                  // items per tile = SEGF_BYTES / sizeof(T)
+constexpr int SEGF_CHUNK = 512;                    // segment offsets staged per round
+constexpr int SEGF_CTAS_PER_SM = 4;
+constexpr uint32_t SEGF_NONE = 0xffffffffu;
+
+struct SegfHdr {
+    unsigned int flag;    // nonzero: use the fallback
+    unsigned int ntiles;
+};
+
+template <typename T>
+struct SegfTemp {
+    SegfHdr* hdr;
+    uint32_t* first;      // [cap + 1] first segment per tile
+    T* carry;             // [cap]
+    uint32_t* carry_seg;  // [cap]
+    T* head;              // [cap]
+    uint32_t* head_seg;   // [cap]
+    uint64_t cap;
+};
+
+template <typename T>
+static size_t segf_bytes_per_tile() { return 2 * sizeof(T) + 3 * sizeof(uint32_t); }
+
+template <typename T>
+static SegfTemp<T> segf_carve(void* temp, size_t bytes) {
+    SegfTemp<T> t{};
+    char* p = (char*)temp;
+    t.hdr = (SegfHdr*)p;
+    const size_t avail = bytes > SEG_HDR + 1024 ? bytes - SEG_HDR - 1024 : 0;
+    t.cap = avail / segf_bytes_per_tile<T>();
+    p += SEG_HDR;
+    t.carry = (T*)p; p += align_up(t.cap * sizeof(T), 8);
+    t.head = (T*)p; p += align_up(t.cap * sizeof(T), 8);
+    t.first = (uint32_t*)p; p += (t.cap + 1) * 4;
+    t.carry_seg = (uint32_t*)p; p += t.cap * 4;
+    t.head_seg = (uint32_t*)p;
+    return t;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+segf_partition_kernel(const uint32_t* __restrict__ begin, const uint32_t* __restrict__ end, uint64_t S,
+                      SegfTemp<T> t) {
+    constexpr uint64_t TI = SEGF_BYTES / sizeof(T);
+    const uint64_t s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= S) return;
+    const uint64_t e = end[s], b = begin[s];
+    const uint64_t pe = s ? end[s - 1] : 0;
+    if (b > e || (s && pe > b)) atomicOr(&t.hdr->flag, 1u);
+    // tiles whose start c*TI lies in [pe, e) begin inside segment s (or its gap)
+    for (uint64_t c = (pe + TI - 1) / TI; c * TI < e; ++c) {
+        if (c >= t.cap) { atomicOr(&t.hdr->flag, 2u); break; }
+        t.first[c] = (uint32_t)s;
+    }
+    if (s == S - 1) {
+        const uint64_t nt = (e + TI - 1) / TI;
+        if (nt == 0 || nt > t.cap) atomicOr(&t.hdr->flag, 2u);  // no items: the fallback writes init
+        else { t.hdr->ntiles = (unsigned)nt; t.first[nt] = (uint32_t)S; }
+    }
+}
+
+// Reduce items [lo, hi) of the staged tile (tile-relative) with one warp.
+template <typename Op, typename T>
+__device__ __forceinline__ T segf_warp_piece(const T* tile, uint32_t lo, uint32_t hi, int lane) {
+    T acc = Op::template identity<T>();
+    for (uint32_t i = lo + lane; i < hi; i += 32) acc = Op::template apply<T>(acc, tile[i]);
+    return warp_reduce<Op>(acc);
+}
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(SEGF_THREADS, SEGF_CTAS_PER_SM)
+segf_main_kernel(const T* __restrict__ in, T* __restrict__ out, const uint32_t* __restrict__ begin,
+                 const uint32_t* __restrict__ end, uint64_t S, T init, SegfTemp<T> t) {
+    constexpr uint32_t TI = SEGF_BYTES / sizeof(T);
+    __shared__ __align__(16) T s_tile[TI];
+    __shared__ uint32_t s_b[SEGF_CHUNK], s_e[SEGF_CHUNK];
+    if (t.hdr->flag) return;
+    const uint64_t ntiles = t.hdr->ntiles;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool vec = (reinterpret_cast<uintptr_t>(in) & 15) == 0;
+    for (uint64_t c = blockIdx.x; c < ntiles; c += gridDim.x) {
+        const uint64_t base = c * TI;
+        // tile items: the last tile ends at the last segment end
+        const uint64_t last_end = end[S - 1];
+        const uint32_t cnt = (uint32_t)min((uint64_t)TI, last_end - base);
+        __syncthreads();  // previous tile fully consumed
+        if (vec && cnt == TI) {
+            constexpr int CH = SEGF_BYTES / 16;
+            for (int k = threadIdx.x; k < CH; k += SEGF_THREADS)
+                cp_async16(reinterpret_cast<char*>(s_tile) + k * 16, reinterpret_cast<const char*>(in + base) + k * 16);
+            cp_async_commit();
+        } else {
+            for (uint32_t k = threadIdx.x; k < cnt; k += SEGF_THREADS) s_tile[k] = in[base + k];
+        }
+        const uint64_t lo = c ? t.first[c] : 0;
+        const uint64_t hi = t.first[c + 1];  // exclusive; segment hi may cross the right edge
+        if (threadIdx.x == 0) { t.carry_seg[c] = SEGF_NONE; t.head_seg[c] = SEGF_NONE; }
+        cp_async_wait_all();
+        __syncthreads();
+        // segments owned by this tile (end inside it), in chunks of offsets
+        for (uint64_t s0 = lo; s0 < hi; s0 += SEGF_CHUNK) {
+            const uint32_t m = (uint32_t)min((uint64_t)SEGF_CHUNK, hi - s0);
+            __syncthreads();
+            for (uint32_t k = threadIdx.x; k < m; k += SEGF_THREADS) { s_b[k] = begin[s0 + k]; s_e[k] = end[s0 + k]; }
+            __syncthreads();
+            for (uint32_t k = warp; k < m; k += SEGF_WARPS) {
+                const uint64_t b = s_b[k], e = s_e[k];
+                const uint32_t plo = b > base ? (uint32_t)(b - base) : 0u;
+                const uint32_t phi = (uint32_t)(e - base);
+                const T v = segf_warp_piece<Op, T>(s_tile, plo, phi > plo ? phi : plo, lane);
+                if (lane == 0) {
+                    if (b >= base || e == b) out[s0 + k] = Op::template apply<T>(init, v);
+                    else { t.head[c] = v; t.head_seg[c] = (uint32_t)(s0 + k); }
+                }
+            }
+        }
+        // the segment crossing the right edge
+        if (warp == 0 && c + 1 < ntiles && hi < S) {
+            const uint64_t b = begin[hi];
+            if (b < base + TI) {
+                const uint32_t plo = b > base ? (uint32_t)(b - base) : 0u;
+                const T v = segf_warp_piece<Op, T>(s_tile, plo, TI, lane);
+                if (lane == 0) { t.carry[c] = v; t.carry_seg[c] = (uint32_t)hi; }
+            }
+        }
+    }
+}
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(256)
+segf_fixup_kernel(T* __restrict__ out, const uint32_t* __restrict__ begin, T init, SegfTemp<T> t) {
+    constexpr uint64_t TI = SEGF_BYTES / sizeof(T);
+    if (t.hdr->flag) return;
+    const uint64_t c = (uint64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (c >= t.hdr->ntiles) return;
+    const uint32_t s = t.head_seg[c];
+    if (s == SEGF_NONE) return;
+    const uint64_t c0 = begin[s] / TI;
+    T acc = Op::template identity<T>();
+    for (uint64_t k = c0 + lane; k < c; k += 32) acc = Op::template apply<T>(acc, t.carry[k]);
+    acc = warp_reduce<Op>(acc);
+    if (lane == 0) out[s] = Op::template apply<T>(Op::template apply<T>(init, acc), t.head[c]);
+}
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(256)
+segf_fallback_kernel(const T* __restrict__ in, T* __restrict__ out, uint64_t S, const uint32_t* __restrict__ begin,
+                     const uint32_t* __restrict__ end, T init, const SegfHdr* hdr) {
+    if (!hdr->flag) return;
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+    for (uint64_t s = (uint64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); s < S; s += warps) {
+        uint64_t b = begin[s], e = end[s];
+        if (e < b) e = b;
+        T acc = Op::template identity<T>();
+        for (uint64_t i = b + lane; i < e; i += 32) acc = Op::template apply<T>(acc, ldcs(in + i));
+        acc = warp_reduce<Op>(acc);
+        if (lane == 0) out[s] = Op::template apply<T>(init, acc);
+    }
+}
+
+template <typename Op, typename T>
+static lcpp_status segf_launch(const void* in, void* out, uint64_t S, const uint32_t* begin, const uint32_t* end,
+                               void* temp, size_t temp_bytes, cudaStream_t s) {
+    const T init = Op::template identity<T>();
+    const SegfTemp<T> t = segf_carve<T>(temp, temp_bytes);
+    const DeviceInfo di = device_info();
+    if (cudaMemsetAsync(t.hdr, 0, sizeof(SegfHdr), s) != cudaSuccess) return LCPP_ERR_CUDA;
+    { ProfScope ps("seg_partition", s);
+    segf_partition_kernel<T><<<(unsigned)ceil_div(S, 256), 256, 0, s>>>(begin, end, S, t); }
+    { ProfScope ps("seg_flat", s);
+    segf_main_kernel<Op, T><<<(unsigned)(di.sms * SEGF_CTAS_PER_SM), SEGF_THREADS, 0, s>>>(
+        (const T*)in, (T*)out, begin, end, S, init, t); }
+    { ProfScope ps("seg_fixup", s);
+    segf_fixup_kernel<Op, T><<<(unsigned)ceil_div(t.cap, 8), 256, 0, s>>>((T*)out, begin, init, t);
+    segf_fallback_kernel<Op, T><<<(unsigned)(di.sms * 4), 256, 0, s>>>((const T*)in, (T*)out, S, begin, end, init,
+                                                                       t.hdr); }
+    count_launch(4);
+    return check_launch();
+}
+
 template <typename Op, typename T>
 static lcpp_status seg_launch(const void* in, void* out, uint64_t S, const uint32_t* begin,
                               const uint32_t* end, uint64_t seg_size, bool fixed, void* temp,
@@ -162,7 +370,15 @@ static lcpp_status seg_launch(const void* in, void* out, uint64_t S, const uint3
 
 template <typename T>
 static lcpp_status seg_op(int op, const void* in, void* out, uint64_t S, const uint32_t* begin,
-                          const uint32_t* end, uint64_t seg_size, bool fixed, void* temp, cudaStream_t s) {
+                          const uint32_t* end, uint64_t seg_size, bool fixed, void* temp, cudaStream_t s,
+                          size_t flat_bytes = 0) {
+    if (flat_bytes) {
+        switch (op) {
+            case LCPP_OP_SUM: return segf_launch<OpSum, T>(in, out, S, begin, end, temp, flat_bytes, s);
+            case LCPP_OP_MIN: return segf_launch<OpMin, T>(in, out, S, begin, end, temp, flat_bytes, s);
+            default: return segf_launch<OpMax, T>(in, out, S, begin, end, temp, flat_bytes, s);
+        }
+    }
     switch (op) {
         case LCPP_OP_SUM: return seg_launch<OpSum, T>(in, out, S, begin, end, seg_size, fixed, temp, s);
         case LCPP_OP_MIN: return seg_launch<OpMin, T>(in, out, S, begin, end, seg_size, fixed, temp, s);
@@ -174,10 +390,19 @@ static lcpp_status seg_op(int op, const void* in, void* out, uint64_t S, const u
 
 using namespace lcpp;
 
+// Temp of the flat path for num_items items (state of every tile plus a spare
+// tile), or at least the long-segment work list of the per-segment path.
+static size_t segf_temp_bytes(size_t es, uint64_t num_items) {
+    const uint64_t tiles = ceil_div(num_items, SEGF_BYTES / es) + 1;
+    return SEG_HDR + 1024 + tiles * (2 * es + 3 * sizeof(uint32_t)) + 256;
+}
+
 extern "C" size_t lcpp_segment_reduce_temp_bytes(int dtype, uint64_t num_items, uint64_t num_segments) {
-    (void)num_items;
-    if (!lcpp_dtype_size(dtype)) return 0;
-    return SEG_HDR + align_up((num_segments ? num_segments : 1) * sizeof(uint32_t), 256);
+    const size_t es = lcpp_dtype_size(dtype);
+    if (!es) return 0;
+    const size_t list = SEG_HDR + align_up((num_segments ? num_segments : 1) * sizeof(uint32_t), 256);
+    const size_t flat = segf_temp_bytes(es, num_items);
+    return list > flat ? list : flat;
 }
 
 extern "C" lcpp_status lcpp_segment_reduce(int op, int dtype, const void* in, void* out,
@@ -187,13 +412,18 @@ extern "C" lcpp_status lcpp_segment_reduce(int op, int dtype, const void* in, vo
     if (op < 0 || op > 2 || !lcpp_dtype_size(dtype)) return LCPP_ERR_INVALID_ARG;
     if (num_segments == 0) return LCPP_OK;
     if (!out || !begin_offsets || !end_offsets || num_segments > 0xffffffffull) return LCPP_ERR_INVALID_ARG;
-    // Without enough temp for the long-segment work list the call still runs:
-    // one warp per segment, long ones included (slower on very long segments).
-    if (!temp || temp_bytes < lcpp_segment_reduce_temp_bytes(dtype, 0, num_segments)) temp = nullptr;
+    // With temp for at least one tile the flat item-tiled path runs (it
+    // checks on the device that the offsets are monotone and that all tiles
+    // fit, else reduces one warp per segment).  With less temp: the
+    // per-segment path, with (or, without room for it, without) the
+    // long-segment work list.
+    const size_t es = lcpp_dtype_size(dtype);
+    const size_t flat = temp && temp_bytes >= segf_temp_bytes(es, 1) ? temp_bytes : 0;
+    if (!flat && (!temp || temp_bytes < SEG_HDR + align_up(num_segments * sizeof(uint32_t), 256))) temp = nullptr;
     return dispatch_dtype(dtype, [&](auto zero) -> lcpp_status {
         using T = decltype(zero);
         return seg_op<T>(op, in, out, num_segments, begin_offsets, end_offsets, 0, false, temp,
-                         (cudaStream_t)stream);
+                         (cudaStream_t)stream, flat);
     });
 }
 

@@ -14,13 +14,14 @@ to shards held in rank order:
 * mg_scan        local reduce -> all-gather of the G shard totals -> carry
                  (sum of lower ranks' totals, in rank order) -> local scan
                  seeded with the carry.  No host synchronisation.
-* mg_sort_pairs  global stable sort: global key range (one all-reduce) ->
-                 one onesweep partition pass on the highest 8 bits that
-                 differ -> all-gathered bucket counts -> contiguous bucket
-                 ranges per rank -> grouped NCCL send/recv -> local onesweep
-                 sort of the bits that differ.  One host synchronisation (the
-                 exchange sizes).  Rank r gets the r-th contiguous slice of the
-                 global order.
+* mg_sort_pairs  global stable sort: 4096 samples per rank of the extended
+                 key (key, rank, index), all-gathered and sorted on the device
+                 -> G-1 splitters -> destination byte per item -> one stable
+                 onesweep pass over those bytes -> grouped NCCL send/recv ->
+                 local onesweep sort of the key bits that differ.  One host
+                 synchronisation (the exchange sizes).  Rank r gets the r-th
+                 contiguous slice of the global order, about n_total/G items
+                 whatever the key distribution.
 
 Scratch comes from a caller temp tensor sized by the *_temp_bytes functions
 (or is allocated once per call when none is passed).  There is no CPU path:
@@ -148,9 +149,10 @@ class SortResult:
 
 
 def default_capacity(n_local: int) -> int:
-    """Output room per rank: slices are balanced to within one partition
-    bucket, so a few percent above the shard size covers uniform keys; skewed
-    keys may need more (the call then raises with ERR_CAPACITY)."""
+    """Output room per rank: the sampled splitters put about n_total/G items
+    on every rank (within a few percent at 4096 samples per rank), so 1/8
+    above the shard size covers even shards; a slice that still does not fit
+    raises with ERR_CAPACITY."""
     return min(n_local + max(n_local // 8, 4096), (1 << 32) - 1)
 
 

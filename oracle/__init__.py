@@ -35,6 +35,7 @@ def lib():
         h.oracle_reduce.argtypes = [i, i, vp, u64, vp]
         h.oracle_scan.argtypes = [i, i, vp, u64, vp]
         h.oracle_abs_prefix_f32.argtypes = [vp, u64, vp]
+        h.oracle_abs_prefix_f64.argtypes = [vp, u64, vp]
         h.oracle_radix_sort.argtypes = [i, i, i, vp, vp, vp, vp, u64, i, i, i]
         h.oracle_segment_reduce.argtypes = [i, i, vp, vp, u64, vp, vp]
         h.oracle_reduce_sum_mt.argtypes = [i, vp, u64, vp, i]
@@ -77,7 +78,8 @@ def reduce(op: int, x: np.ndarray):
 
 
 def scan(inclusive: bool, x: np.ndarray) -> np.ndarray:
-    """u32/i32: exact wrapped prefixes in x.dtype.  f32: fp64 prefixes."""
+    """Integers: exact wrapped prefixes in x.dtype.  f32: fp64 prefixes.
+    f64: prefixes accumulated in long double, rounded to fp64."""
     x = np.ascontiguousarray(x)
     out = np.empty(x.size, dtype=np.float64 if x.dtype == np.float32 else x.dtype)
     _ok(lib().oracle_scan(int(inclusive), _dt(x), _p(x), x.size, _p(out)), "scan")
@@ -85,6 +87,12 @@ def scan(inclusive: bool, x: np.ndarray) -> np.ndarray:
 
 
 def abs_prefix(x: np.ndarray) -> np.ndarray:
+    """Running sum of |x| in fp64 (the scale of the float-scan tolerance)."""
+    if x.dtype == np.float64:
+        x = np.ascontiguousarray(x)
+        out = np.empty(x.size, dtype=np.float64)
+        lib().oracle_abs_prefix_f64(_p(x), x.size, _p(out))
+        return out
     x = np.ascontiguousarray(x, dtype=np.float32)
     out = np.empty(x.size, dtype=np.float64)
     lib().oracle_abs_prefix_f32(_p(x), x.size, _p(out))

@@ -203,17 +203,19 @@ def refgen(case: str, n: int = 0) -> dict:
 
 # ---- tolerances --------------------------------------------------------------
 def assert_float_sum_close(y, ref_fp64, abs_scale, rel=1e-5):
-    """|y - ref| <= rel * max(|ref|, abs_scale * 2^-10): fp32 results within
+    """|y - ref| <= rel * max(|ref|, abs_scale * 2^-6): fp32 results within
     1e-5 relative of an fp64 oracle, with the relative scale floored at
-    2^-10 of the running sum of |x| (abs_scale) where prefixes cross zero.
+    1/64 of the running sum of |x| (abs_scale) where prefixes cross zero.
     The floor is the conditioning term of floating-point summation: any fp32
-    summation order (sequential included) carries an error proportional to
-    eps32 * sum|x|, which a pure |ref|-relative bound cannot absorb near 0.
-    Measured on B200 for the N(0,1) InclusiveSum / ExclusiveSum at 2^24,
-    2^26 and 2^28 items: the largest error / bound ratio is 0.70."""
+    summation order (sequential included) carries an error of order
+    u * sum|x| (u = 2^-24), so the floor must exceed u / rel ~ 2^-7.4; 2^-6
+    is the smallest power of two above that.  Measured on B200: the N(0,1)
+    InclusiveSum / ExclusiveSum at 2^24-2^28 items stay at 0.08 of this
+    bound, and a 2^-10 floor is exceeded (ratio 1.2 at item 109 of the
+    float scan tests' input)."""
     y = np.asarray(y, dtype=np.float64)
     ref = np.asarray(ref_fp64, dtype=np.float64)
-    scale = np.maximum(np.abs(ref), np.asarray(abs_scale, dtype=np.float64) * 2.0 ** -10)
+    scale = np.maximum(np.abs(ref), np.asarray(abs_scale, dtype=np.float64) * 2.0 ** -6)
     err = np.abs(y - ref)
     bad = err > rel * scale + 1e-30
     if bad.any():

@@ -37,7 +37,8 @@ def test_temp_sizes():
     assert lib.lcpp_reduce_temp_bytes(L.I32, 1 << 24) > 0
     assert lib.lcpp_reduce_temp_bytes(L.NONE, 10) == 0
     assert lib.lcpp_scan_temp_bytes(L.U32, 1 << 28) >= 8 * (1 << 28) // 8192
-    assert lib.lcpp_scan_temp_bytes(L.U64, 10) == 0  # scan serves 4-byte types
+    assert lib.lcpp_scan_temp_bytes(L.U64, 1 << 28) > lib.lcpp_scan_temp_bytes(L.U32, 1 << 28)  # 8-byte descriptors
+    assert lib.lcpp_scan_temp_bytes(L.NONE, 10) == 0
     n = 1 << 28
     pairs = lib.lcpp_radix_sort_temp_bytes(L.U32, L.U32, n)
     keys = lib.lcpp_radix_sort_temp_bytes(L.U32, L.NONE, n)
@@ -54,7 +55,7 @@ def test_argument_validation_without_device():
     assert lib.lcpp_reduce(0, 99, bad, bad, 10, bad, 1 << 20, None) == L.ERR_INVALID_ARG
     assert lib.lcpp_reduce(0, L.I32, bad, bad, 10, bad, 16, None) == L.ERR_TEMP_TOO_SMALL
     assert lib.lcpp_scan(5, L.U32, bad, bad, 10, bad, 1 << 20, None) == L.ERR_INVALID_ARG
-    assert lib.lcpp_scan(0, L.F64, bad, bad, 10, bad, 1 << 20, None) == L.ERR_INVALID_ARG
+    assert lib.lcpp_scan(0, L.NONE, bad, bad, 10, bad, 1 << 20, None) == L.ERR_INVALID_ARG
     assert lib.lcpp_scan(0, L.U32, bad, bad, 0, None, 0, None) == L.OK  # n = 0: nothing to do
     assert lib.lcpp_scan(0, L.U32, bad, bad, 1 << 20, bad, 8, None) == L.ERR_TEMP_TOO_SMALL
     assert lib.lcpp_radix_sort(L.NONE, L.NONE, 0, bad, bad, None, None, 10, 0, 0, bad, 1 << 30, None) == L.ERR_INVALID_ARG

@@ -55,6 +55,30 @@ def test_float_scan_tolerance(cuda, inclusive):
         assert_float_sum_close(got, oracle.scan(inclusive, x), oracle.abs_prefix(x))
 
 
+@pytest.mark.parametrize("inclusive", [False, True])
+@pytest.mark.parametrize("dtype", [np.uint64, np.int64])
+def test_integer_scan_8byte_bit_exact(cuda, inclusive, dtype):
+    # The reference's NumericT scans (device_scan.h:180-204) admit 8-byte types.
+    for i, n in enumerate(SIZES + [3 * 4096 + 5, 4096, 16384 + 1]):
+        x = G.u64(n, seed=150 + i).view(dtype)  # full range: exercises wraparound
+        got = abi_scan(inclusive, x, offset_elems=i % 3)
+        assert np.array_equal(got, oracle.scan(inclusive, x)), n
+
+
+@pytest.mark.parametrize("inclusive", [False, True])
+def test_double_scan_tolerance(cuda, inclusive):
+    for i, n in enumerate(SIZES):
+        x = G.f32_normal(n, seed=250 + i).astype(np.float64) * np.float64(1.0 + 1e-9)
+        got = abi_scan(inclusive, x, offset_elems=i % 2)
+        assert_float_sum_close(got, oracle.scan(inclusive, x), oracle.abs_prefix(x), rel=1e-12)
+
+
+def test_8byte_scan_full_size(cuda):
+    # 2^27 uint64 (1 GiB): bit-exact against the oracle.
+    x = G.u64(1 << 27, seed=3)
+    assert np.array_equal(abi_scan(False, x), oracle.scan(False, x))
+
+
 def test_in_place(cuda):
     x = G.u32_below(123457, 16, seed=7)
     got = abi_scan(False, x, in_place=True)

@@ -110,3 +110,65 @@ def test_config4_full_size(cuda):
     want = oracle.segment_reduce(2, xi, b, e)
     assert np.array_equal(got, want)
     assert (got[b == e] == np.iinfo(np.int32).min).all()
+
+
+def _abi_seg_custom(op, x, b, e, temp_items=None, offset_elems=0):
+    """lcpp_segment_reduce with the temp of lcpp_segment_reduce_temp_bytes(temp_items)
+    (default: the real item count) and, optionally, an unaligned input view."""
+    import torch
+
+    from lc_parallel_primitive_b200 import _lib as L
+    from tests.helpers import NP2LCPP, empty_dev, stream, temp, to_dev, to_host
+
+    lib = L.lib()
+    dt = NP2LCPP[x.dtype]
+    d = to_dev(x, offset_elems)
+    db, de = to_dev(b.astype(np.uint32)), to_dev(e.astype(np.uint32))
+    out = empty_dev(b.size, x.dtype)
+    tb = lib.lcpp_segment_reduce_temp_bytes(dt, x.size if temp_items is None else temp_items, b.size)
+    t = temp(tb)
+    L.check(lib.lcpp_segment_reduce(op, dt, d.data_ptr(), out.data_ptr(), b.size, db.data_ptr(), de.data_ptr(),
+                                    t.data_ptr(), tb, stream()))
+    torch.cuda.synchronize()
+    L.check(lib.lcpp_last_device_error(stream()))
+    return to_host(out)
+
+
+def test_flat_path_offsets_that_are_not_csr(cuda):
+    N = 200003
+    xi = G.u32(N, seed=21).view(np.int32)
+    rng = np.random.default_rng(21)
+    # gaps between segments and a first segment that does not start at 0
+    cuts = np.sort(rng.choice(np.arange(1, N), size=2 * 999, replace=False)).astype(np.uint32)
+    b, e = cuts[0::2], cuts[1::2]
+    for op in (0, 1, 2):
+        assert np.array_equal(_abi_seg_custom(op, xi, b, e), oracle.segment_reduce(op, xi, b, e))
+    # overlapping and unordered segments: the device check sends them to the per-segment kernel
+    b2 = rng.integers(0, N - 5000, size=777).astype(np.uint32)
+    e2 = (b2 + rng.integers(0, 5000, size=777)).astype(np.uint32)
+    for op in (0, 2):
+        assert np.array_equal(_abi_seg_custom(op, xi, b2, e2), oracle.segment_reduce(op, xi, b2, e2))
+
+
+def test_flat_path_edges(cuda):
+    xi = G.u32(1 << 20, seed=22).view(np.int32)
+    # all segments empty (no tiles): every output is init
+    z = np.zeros(1000, dtype=np.uint32)
+    assert np.array_equal(_abi_seg_custom(2, xi[:0], z, z), np.full(1000, np.iinfo(np.int32).min, np.int32))
+    # one segment over many tiles, with empty segments around it, and an exact tile edge
+    TI = 8192
+    lens = np.array([0, 5 * TI + 17, 0, 0, TI - 17, TI, 1, 0, 3 * TI], dtype=np.uint64)
+    off = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+    x = xi[: int(off[-1])]
+    b, e = off[:-1], off[1:]
+    for op in (0, 1, 2):
+        assert np.array_equal(_abi_seg_custom(op, x, b, e), oracle.segment_reduce(op, x, b, e))
+    # temp sized for fewer items than the offsets reach: the device check falls back
+    assert np.array_equal(_abi_seg_custom(0, x, b, e, temp_items=1), oracle.segment_reduce(0, x, b, e))
+    # an input that is not 16-byte aligned (scalar tile loads)
+    xf = G.f32_unit(int(off[-1]), seed=23)
+    got = _abi_seg_custom(0, xf, b, e, offset_elems=1)
+    np.testing.assert_allclose(got.astype(np.float64), oracle.segment_reduce(0, xf, b, e), rtol=1e-5, atol=0)
+    # 8-byte values (4096-item tiles)
+    x8 = G.u64(int(off[-1]), seed=24).view(np.int64)
+    assert np.array_equal(_abi_seg_custom(0, x8, b, e), oracle.segment_reduce(0, x8, b, e))
