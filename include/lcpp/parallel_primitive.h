@@ -9,3 +9,4 @@
 #include "lcpp/device/device_scan.h"
 #include "lcpp/device/device_radix_sort.h"
 #include "lcpp/device/device_segment_reduce.h"
+#include "lcpp/device/device_multi_gpu.h"

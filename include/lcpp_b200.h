@@ -169,7 +169,10 @@ lcpp_status lcpp_segment_reduce_fixed(int op, int dtype, const void* in, void* o
  * returns LCPP_ERR_INVALID_ARG.  The array is shared by all calls on a device:
  * calls that overlap on the GPU race and must be serialized.  The first call
  * on a device looks up the array's address (cudaGetSymbolAddress); make it
- * before any stream capture.  Allocates nothing. */
+ * before any stream capture (made during capture it returns
+ * LCPP_ERR_UNSUPPORTED).  The address is kept per device ordinal, so
+ * cudaDeviceReset while the library is loaded is not supported.  Allocates
+ * nothing. */
 uint64_t    lcpp_scan_noalloc_max_items(void);
 lcpp_status lcpp_scan_noalloc(int kind, int dtype, const void* in, void* out, uint64_t n,
                               void* stream);

@@ -226,6 +226,24 @@ constexpr size_t rs_smem_bytes() {
 }
 
 
+// Coalesced copy of items [base, base + count) (16-byte vectors when aligned).
+template <typename E>
+__device__ __forceinline__ void rs_copy_tile(const void* src, void* dst, uint64_t base, uint32_t count, int tid,
+                                             int threads) {
+    const E* s = reinterpret_cast<const E*>(src) + base;
+    E* d = reinterpret_cast<E*>(dst) + base;
+    constexpr uint32_t V = 16 / sizeof(E);
+    const bool vec = ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15) == 0;
+    uint32_t done = 0;
+    if (vec) {
+        const uint32_t nv = count / V;
+        for (uint32_t i = tid; i < nv; i += threads)
+            __stcs(reinterpret_cast<uint4*>(d) + i, ld_stream(reinterpret_cast<const uint4*>(s) + i));
+        done = nv * V;
+    }
+    for (uint32_t i = done + tid; i < count; i += threads) stcs(d + i, ldcs(s + i));
+}
+
 template <typename KB, typename VB, typename W, int KIND, bool DESC, int THREADS, bool DIG = false>
 __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(RsPass a) {
     constexpr int RS_WARPS = THREADS / 32;
@@ -248,11 +266,24 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) s_misc[0] = atomicAdd(a.ticket, 1u);
     for (int i = tid; i < RS_WARPS * RS_DIGITS; i += THREADS) s_wc[i] = s_wm[i] = 0;
-    __syncthreads();
+    // A pass in which one digit holds every item is the identity permutation
+    // (skewed keys: e.g. the high digits of keys with 8 bits of entropy).
+    bool one_digit = false;
+    if (tid < RS_DIGITS) {
+        const uint32_t lo = a.bins[tid];
+        const uint32_t hi = tid + 1 < RS_DIGITS ? a.bins[tid + 1] : (uint32_t)a.n;
+        one_digit = (uint64_t)(hi - lo) == a.n;
+    }
+    const bool identity_pass = __syncthreads_or(one_digit);
     const uint64_t tile = s_misc[0];
     const uint64_t tile_base = tile * TILE;
     const uint64_t rem = a.n - tile_base;
     const uint32_t num_valid = rem < (uint64_t)TILE ? (uint32_t)rem : (uint32_t)TILE;
+    if (identity_pass) {  // straight copy of the tile; no ranking, no look-back
+        rs_copy_tile<KB>(a.keys_in, a.keys_out, tile_base, num_valid, tid, THREADS);
+        if constexpr (HAS_V) rs_copy_tile<VB>(a.vals_in, a.vals_out, tile_base, num_valid, tid, THREADS);
+        return;
+    }
 
     const KB* kin = reinterpret_cast<const KB*>(a.keys_in);
     const uint32_t wbase = (uint32_t)warp * (ITEMS * 32);

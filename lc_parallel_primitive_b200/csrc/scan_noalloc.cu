@@ -22,6 +22,8 @@
 //    cudaGetSymbolAddress (with that device current); make that first call
 //    before any stream capture.
 #include "common.cuh"
+#include <mutex>
+#include <vector>
 
 namespace lcpp {
 
@@ -30,13 +32,26 @@ constexpr size_t SCAN_NOALLOC_BYTES = SCAN_HDR + SCAN_NOALLOC_MAX_TILES * sizeof
 
 static __device__ __align__(256) unsigned char g_scan_noalloc_scratch[SCAN_NOALLOC_BYTES];
 
-// Device address of g_scan_noalloc_scratch for `dev` (looked up once).
-static lcpp_status scan_noalloc_scratch(int dev, void** out) {
+// Device address of g_scan_noalloc_scratch for `dev` (looked up once per
+// device ordinal; the table is sized by cudaGetDeviceCount).  The cache
+// assumes the device is not reset (cudaDeviceReset) while the library is
+// loaded.  A first lookup while `stream` is being captured into a graph
+// returns LCPP_ERR_UNSUPPORTED: make the first call on each device outside
+// capture.
+static lcpp_status scan_noalloc_scratch(int dev, cudaStream_t stream, void** out) {
     static std::mutex mu;
-    static void* addr[64] = {};
-    if (dev < 0 || dev >= 64) return LCPP_ERR_INVALID_ARG;
+    static std::vector<void*> addr;
     std::lock_guard<std::mutex> g(mu);
+    if (addr.empty()) {
+        int count = 0;
+        if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) return LCPP_ERR_CUDA;
+        addr.assign((size_t)count, nullptr);
+    }
+    if (dev < 0 || (size_t)dev >= addr.size()) return LCPP_ERR_INVALID_ARG;
     if (!addr[dev]) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) return LCPP_ERR_CUDA;
+        if (cs != cudaStreamCaptureStatusNone) return LCPP_ERR_UNSUPPORTED;
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_scan_noalloc_scratch) != cudaSuccess || !p) return LCPP_ERR_CUDA;
         addr[dev] = p;
@@ -61,7 +76,7 @@ extern "C" lcpp_status lcpp_scan_noalloc(int kind, int dtype, const void* in, vo
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return LCPP_ERR_CUDA;
     void* scratch = nullptr;
-    const lcpp_status st = scan_noalloc_scratch(dev, &scratch);
+    const lcpp_status st = scan_noalloc_scratch(dev, (cudaStream_t)stream, &scratch);
     if (st != LCPP_OK) return st;
     const uint64_t tiles = ceil_div(n, SCAN_TILE);
     cudaStream_t s = (cudaStream_t)stream;

@@ -336,6 +336,56 @@ int main(int argc, char* argv[]) {
         }
     }
 
+    // ---- MultiDevice (multi-GPU extension) on a 1-rank NCCL communicator -----
+    {
+        std::vector<char> uid(lcpp_mg_unique_id_bytes());
+        void* comm = nullptr;
+        if (lcpp_mg_get_unique_id(uid.data()) == LCPP_OK && lcpp_mg_comm_init_rank(&comm, 1, uid.data(), 0) == LCPP_OK) {
+            MultiDevice mg;
+            mg.create(device, comm, &stream);
+            const uint n = 300007;
+            std::vector<uint64_t> keys(n);
+            std::vector<uint> vals(n);
+            std::mt19937_64 rng(114521);
+            for (uint j = 0; j < n; j++) { keys[j] = rng() & 0xFFFFFull; vals[j] = j; }
+            auto kin = device.create_buffer<uint64_t>(n), kout = device.create_buffer<uint64_t>(n);
+            auto vin = device.create_buffer<uint>(n), vout = device.create_buffer<uint>(n);
+            stream << kin.copy_from(keys.data()) << vin.copy_from(vals.data()) << synchronize();
+            auto temp = device.create_buffer<uint>(
+                bytes_to_uint_count(MultiDevice::GetSortPairsTempStorageBytes<uint64_t, uint>(n, n, 1)));
+            uint64_t n_out = 0;
+            CommandList cmdlist;
+            mg.SortPairs(cmdlist, temp.view(), kin.view(), kout.view(), vin.view(), vout.view(), n, n, &n_out);
+            std::vector<uint64_t> ko(n);
+            std::vector<uint> vo(n);
+            stream << cmdlist.commit() << synchronize() << kout.copy_to(ko.data()) << vout.copy_to(vo.data())
+                   << synchronize();
+            std::vector<uint> idx(n);
+            std::iota(idx.begin(), idx.end(), 0u);
+            std::stable_sort(idx.begin(), idx.end(), [&](uint a, uint b) { return keys[a] < keys[b]; });
+            int bad = 0;
+            for (uint j = 0; j < n; j++) bad += ko[j] != keys[idx[j]] || vo[j] != idx[j];
+            EXPECT(n_out == n && bad == 0, "MultiDevice SortPairs: n_out %llu, %d wrong", (unsigned long long)n_out, bad);
+            auto sin = device.create_buffer<uint>(n), sout = device.create_buffer<uint>(n), red = device.create_buffer<uint>(1);
+            stream << sin.copy_from(vals.data()) << synchronize();
+            auto st = device.create_buffer<uint>(bytes_to_uint_count(
+                std::max(MultiDevice::GetScanTempStorageBytes<uint>(n, 1), MultiDevice::GetReduceTempStorageBytes<uint>(n))));
+            mg.ExclusiveSum(cmdlist, st.view(), sin.view(), sout.view(), n);
+            stream << cmdlist.commit() << synchronize();
+            mg.Max(cmdlist, st.view(), sin.view(), red.view(), n);
+            std::vector<uint> so(n), rmax(1);
+            stream << cmdlist.commit() << synchronize() << sout.copy_to(so.data()) << red.copy_to(rmax.data())
+                   << synchronize();
+            bad = 0;
+            uint acc = 0;
+            for (uint j = 0; j < n; j++) { bad += so[j] != acc; acc += vals[j]; }
+            EXPECT(bad == 0 && rmax[0] == n - 1, "MultiDevice ExclusiveSum/Max: %d wrong, max %u", bad, rmax[0]);
+            lcpp_mg_comm_destroy(comm);
+        } else {
+            EXPECT(false, "could not make a 1-rank NCCL communicator");
+        }
+    }
+
     EXPECT(stream.last_status() == 0, "stream status %d", stream.last_status());
     std::printf("%s: %d failure(s)\n", g_failures ? "FAILED" : "OK", g_failures);
     return g_failures ? 1 : 0;

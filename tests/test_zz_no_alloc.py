@@ -14,12 +14,12 @@ from tests.helpers import abi_scan, assert_float_sum_close, empty_dev, stream, t
 pytestmark = pytest.mark.gpu
 
 
-def _noalloc(kind, x):
+def _noalloc(kind, x, offset_elems=0, in_place=False):
     import torch
 
     lib = L.lib()
-    d = to_dev(x)
-    out = empty_dev(x.size, x.dtype)
+    d = to_dev(x, offset_elems)
+    out = d if in_place else empty_dev(x.size, x.dtype, offset_elems)
     dt = {np.dtype(np.uint32): L.U32, np.dtype(np.int32): L.I32, np.dtype(np.float32): L.F32}[x.dtype]
     L.check(lib.lcpp_scan_noalloc(kind, dt, d.data_ptr(), out.data_ptr(), x.size, stream()))
     torch.cuda.synchronize()
@@ -40,6 +40,30 @@ def test_noalloc_scan_matches_regular_scan(cuda):
     import oracle
 
     assert_float_sum_close(got, ref.astype(np.float64), oracle.abs_prefix(f))
+
+
+def test_noalloc_allocates_nothing_and_serves_odd_buffers(cuda):
+    # Warm call first (module and array already resident), then device memory
+    # in use must not change across further calls; unaligned and in-place
+    # buffers take the tile kernel's scalar path.
+    import torch
+
+    x = G.u32_below(777777, 1 << 12, seed=44)
+    want = abi_scan(False, x)
+    assert np.array_equal(_noalloc(0, x), want)
+    d = to_dev(x, 1)
+    out = empty_dev(x.size, x.dtype, 3)
+    lib = L.lib()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        L.check(lib.lcpp_scan_noalloc(0, L.U32, d.data_ptr(), out.data_ptr(), x.size, stream()))
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    assert np.array_equal(to_host(out), want)
+    assert np.array_equal(_noalloc(0, x, in_place=True), want)
+    assert np.array_equal(_noalloc(1, x, offset_elems=2), abi_scan(True, x))
 
 
 def test_noalloc_rejects_oversize(cuda):
