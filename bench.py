@@ -351,6 +351,9 @@ def main():
                          "achieved": os_achieved, "peak": peak, "unit": "GB/s", "frac": os_achieved / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                          "traffic": TRAFFIC_PER_PAIR_PASS * n if TRAFFIC_PER_PAIR_PASS else None,
+                         "traffic_source": "ncu dram__bytes_read+write of one onesweep launch at 2^26 pairs "
+                                           "(profiles/dram_traffic_sort_scan_2p26.md), 15.25 B per pair, scaled "
+                                           "to 2^28 pairs by the pair count",
                          "avg_launch_ms": os_avg_ms, "bytes_per_launch": os_bytes,
                          "whole_sort_frac": (68 * n / (ms * 1e-3) / 1e9) / peak},
             "kernels": {k: {"launches": c, "total_ms": t} for k, (c, t) in prof.items()},
@@ -526,7 +529,7 @@ def run_extras(torch, dev, lib, L, G, peak, rank, world, max_over_ranks, barrier
     lib.lcpp_profile_enable(1)  # per-kernel times in a separate untimed pass
     timeit(seg, 10)
     kern = {}
-    for kname in ("seg_warp", "seg_block"):
+    for kname in ("seg_partition", "seg_flat", "seg_fixup"):
         c, tt = L.C.c_uint64(0), L.C.c_double(0)
         lib.lcpp_profile_read(kname.encode(), L.C.byref(c), L.C.byref(tt))
         kern[kname + "_avg_ms"] = float(tt.value) / max(int(c.value), 1)
@@ -624,7 +627,9 @@ def run_mg_extras(torch, dev, lib, L, peak, rank, world, max_over_ranks, barrier
         for nm in names:
             c, t = L.C.c_uint64(0), L.C.c_double(0)
             lib.lcpp_profile_read(nm.encode(), L.C.byref(c), L.C.byref(t))
-            res[nm + "_ms"] = max_over_ranks(float(t.value) / max(int(c.value), 1))
+            v = max_over_ranks(float(t.value) / max(int(c.value), 1))
+            if c.value or world > 1:
+                res[nm + "_ms"] = v
         return res
 
     def timed(fn, k):
