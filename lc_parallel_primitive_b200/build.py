@@ -60,8 +60,9 @@ def _unit_deps(unit: str):
 
 
 def build_library(force: bool = False, verbose: bool = False) -> Path:
-    """Compile the units as relocatable device code in parallel (only those
-    whose sources changed), then device-link them into liblcpp_b200.so."""
+    """Compile the units in parallel (only those whose sources changed), then
+    link them into liblcpp_b200.so.  Each unit is whole-program device code
+    (no -rdc): the units share no device symbols."""
     from concurrent.futures import ThreadPoolExecutor
 
     all_deps = sorted({d for u in UNITS for d in _unit_deps(u)})
@@ -74,7 +75,7 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
     def compile_unit(uo):
         u, o = uo
         tmp = o.with_suffix(".o.tmp")
-        _run([_nvcc(), *NVCC_ARCH, "-lineinfo", "-O3", "-std=c++17", "-rdc=true", "-Xcompiler", "-fPIC",
+        _run([_nvcc(), *NVCC_ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
               f"-I{INCLUDE}", "-c", CSRC / f"{u}.cu", "-o", tmp], verbose)
         os.replace(tmp, o)
 
@@ -82,7 +83,7 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
         list(ex.map(compile_unit, todo))
     if force or todo or _stale(LIB, objs):
         tmp = LIB.with_suffix(".so.tmp")
-        _run([_nvcc(), *NVCC_ARCH, "-shared", "-rdc=true", "-Xcompiler", "-fPIC", *objs, "-o", tmp, "-ldl"],
+        _run([_nvcc(), *NVCC_ARCH, "-shared", "-Xcompiler", "-fPIC", *objs, "-o", tmp, "-ldl"],
              verbose)
         os.replace(tmp, LIB)
     return LIB

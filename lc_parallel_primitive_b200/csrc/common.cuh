@@ -14,10 +14,31 @@ constexpr int WARP = 32;
 // ---------------------------------------------------------------------------
 // Device-side error word and look-back wait cap (one per device, per process).
 // ---------------------------------------------------------------------------
-// Defined once, in runtime.cu; the units are compiled as relocatable device
-// code and device-linked into one library, so every kernel sees one copy.
-extern __device__ unsigned int g_error;        // first latched lcpp_status (as unsigned)
-extern __device__ unsigned int g_spin_limit;   // polls before a wait gives up (~1 s)
+// The library is built from a few compilation units (whole-program device
+// code in each, no relocatable device code, which slowed the short two-kernel
+// reduce by 16 us).  Each unit has its own copy of these words; every unit
+// registers a host hook, and lcpp_last_device_error / lcpp_set_spin_limit
+// walk all of them.
+static __device__ unsigned int g_error = 0;               // first latched lcpp_status (as unsigned)
+static __device__ unsigned int g_spin_limit = 1u << 22;   // polls before a wait gives up (~1 s)
+
+// op 0: read this unit's error word into *value and clear it (async on s);
+// op 1: set this unit's spin limit to *value.
+using UnitHook = int (*)(int op, unsigned int* value, cudaStream_t s);
+void register_unit_hook(UnitHook hook);  // runtime.cu
+static int unit_words_hook(int op, unsigned int* value, cudaStream_t s) {
+    if (op == 0) {
+        const unsigned int zero = 0;
+        if (cudaMemcpyFromSymbolAsync(value, g_error, sizeof(unsigned int), 0, cudaMemcpyDeviceToHost, s) !=
+                cudaSuccess ||
+            cudaMemcpyToSymbolAsync(g_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess)
+            return -1;
+        return 0;
+    }
+    return cudaMemcpyToSymbol(g_spin_limit, value, sizeof(unsigned int)) == cudaSuccess ? 0 : -1;
+}
+static const int unit_words_registered = (register_unit_hook(unit_words_hook), 0);
 
 __device__ __forceinline__ void set_error(int status) {
     atomicCAS(&g_error, 0u, (unsigned int)status);
@@ -85,6 +106,11 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
     const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
 }
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_prior1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 

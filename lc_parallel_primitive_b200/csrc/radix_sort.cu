@@ -141,12 +141,16 @@ rs_histogram_cols_kernel(const KB* __restrict__ keys, uint64_t n, uint32_t* __re
     }
 }
 
-// In-place exclusive scan of each pass's 256 counts (one CTA per pass).
-__global__ void __launch_bounds__(RS_DIGITS) rs_bins_scan_kernel(uint32_t* bins) {
+// In-place exclusive scan of each pass's 256 counts (one CTA per pass), and
+// identity[p] = 1 when one digit of pass p holds all n items (the pass is
+// then the identity permutation).
+__global__ void __launch_bounds__(RS_DIGITS) rs_bins_scan_kernel(uint32_t* bins, uint64_t n, uint32_t* identity) {
     __shared__ uint32_t s_w[RS_DIGITS / 32];
     uint32_t* b = bins + blockIdx.x * RS_DIGITS;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t c = b[threadIdx.x];
+    const int one_digit = __syncthreads_or((uint64_t)c == n);
+    if (threadIdx.x == 0) identity[blockIdx.x] = one_digit ? 1u : 0u;
     uint32_t incl = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -214,6 +218,7 @@ struct RsPass {
     const uint32_t* bins;   // 256 global digit starts of this pass
     void* lookback;         // tiles x 256 words, zeroed
     uint32_t* ticket;       // zeroed
+    const uint32_t* identity;  // nonzero: this pass is the identity permutation
     const uint8_t* digits;      // DIG kernels: precomputed digit of every item (no key bits used)
 };
 
@@ -266,24 +271,15 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) s_misc[0] = atomicAdd(a.ticket, 1u);
     for (int i = tid; i < RS_WARPS * RS_DIGITS; i += THREADS) s_wc[i] = s_wm[i] = 0;
-    // A pass in which one digit holds every item is the identity permutation
-    // (skewed keys: e.g. the high digits of keys with 8 bits of entropy).
-    bool one_digit = false;
-    if (tid < RS_DIGITS) {
-        const uint32_t lo = a.bins[tid];
-        const uint32_t hi = tid + 1 < RS_DIGITS ? a.bins[tid + 1] : (uint32_t)a.n;
-        one_digit = (uint64_t)(hi - lo) == a.n;
-    }
-    const bool identity_pass = __syncthreads_or(one_digit);
+    // A pass in which one digit holds every item (skewed keys: e.g. the high
+    // digits of keys with 8 bits of entropy) is the identity permutation.  The
+    // flag is loaded now and looked at once the keys are in registers.
+    const uint32_t identity_pass = *a.identity;
+    __syncthreads();
     const uint64_t tile = s_misc[0];
     const uint64_t tile_base = tile * TILE;
     const uint64_t rem = a.n - tile_base;
     const uint32_t num_valid = rem < (uint64_t)TILE ? (uint32_t)rem : (uint32_t)TILE;
-    if (identity_pass) {  // straight copy of the tile; no ranking, no look-back
-        rs_copy_tile<KB>(a.keys_in, a.keys_out, tile_base, num_valid, tid, THREADS);
-        if constexpr (HAS_V) rs_copy_tile<VB>(a.vals_in, a.vals_out, tile_base, num_valid, tid, THREADS);
-        return;
-    }
 
     const KB* kin = reinterpret_cast<const KB*>(a.keys_in);
     const uint32_t wbase = (uint32_t)warp * (ITEMS * 32);
@@ -294,6 +290,16 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     for (int i = 0; i < ITEMS; ++i) {
         const uint32_t li = wbase + i * 32 + lane;
         key[i] = li < num_valid ? ldcs(kin + tile_base + li) : KB(0);
+    }
+    if (identity_pass) {  // keys back out where they came from, values copied; no rank, no look-back
+        KB* kout0 = reinterpret_cast<KB*>(a.keys_out);
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {
+            const uint32_t li = wbase + i * 32 + lane;
+            if (li < num_valid) stcs(kout0 + tile_base + li, key[i]);
+        }
+        if constexpr (HAS_V) rs_copy_tile<VB>(a.vals_in, a.vals_out, tile_base, num_valid, tid, THREADS);
+        return;
     }
     uint32_t dg[DIG ? ITEMS : 1];
     if constexpr (DIG) {
@@ -555,7 +561,7 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
         else
             hk<<<(unsigned)g, HISTC_THREADS, hsmem, s>>>((const KB*)keys_in, n, bins, begin_bit, end_bit, L.passes); }
         { ProfScope ps("rs_bins_scan", s);
-        rs_bins_scan_kernel<<<L.passes, RS_DIGITS, 0, s>>>(bins); }
+        rs_bins_scan_kernel<<<L.passes, RS_DIGITS, 0, s>>>(bins, n, tickets + RS_MAX_PASSES); }
         count_launch(2);
     }
     const int threads = digits ? RS_THREADS : rs_threads();
@@ -597,6 +603,7 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
         a.bins = bins + p * RS_DIGITS;
         a.lookback = lb + (size_t)p * L.tiles * RS_DIGITS * L.lb_word;
         a.ticket = tickets + p;
+        a.identity = tickets + RS_MAX_PASSES + p;
         a.digits = digits;
         { ProfScope ps("rs_onesweep", s);
         kern<<<(unsigned)L.tiles, threads, smem, s>>>(a); }

@@ -2,12 +2,17 @@
 // device attribute cache, launch counter and small ABI helpers.
 #include "common.cuh"
 #include <mutex>
+#include <vector>
 
 namespace lcpp {
 
-__device__ unsigned int g_error = 0;
-__device__ unsigned int g_spin_limit = 1u << 22;
 
+
+static std::vector<UnitHook>& unit_hooks() {
+    static std::vector<UnitHook> hooks;
+    return hooks;
+}
+void register_unit_hook(UnitHook hook) { unit_hooks().push_back(hook); }
 
 DeviceInfo device_info() {
     static std::mutex mu;
@@ -57,18 +62,19 @@ extern "C" size_t lcpp_dtype_size(int dtype) {
 
 extern "C" lcpp_status lcpp_last_device_error(void* stream) {
     cudaStream_t s = (cudaStream_t)stream;
-    unsigned int err = 0, zero = 0;
-    if (cudaMemcpyFromSymbolAsync(&err, g_error, sizeof(err), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess)
-        return LCPP_ERR_CUDA;
-    if (cudaMemcpyToSymbolAsync(g_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) != cudaSuccess)
-        return LCPP_ERR_CUDA;
-    if (cudaStreamSynchronize(s) != cudaSuccess) return LCPP_ERR_CUDA;
-    return (lcpp_status)(int)err;
+    unsigned int first = 0;
+    for (UnitHook h : unit_hooks()) {  // every unit's word, each read and cleared
+        unsigned int err = 0;
+        if (h(0, &err, s) != 0) return LCPP_ERR_CUDA;
+        if (!first) first = err;
+    }
+    return (lcpp_status)(int)first;
 }
 
 extern "C" lcpp_status lcpp_set_spin_limit(uint32_t iterations) {
-    const unsigned int v = iterations ? iterations : (1u << 22);
-    if (cudaMemcpyToSymbol(g_spin_limit, &v, sizeof(v)) != cudaSuccess) return LCPP_ERR_CUDA;
+    unsigned int v = iterations ? iterations : (1u << 22);
+    for (UnitHook h : unit_hooks())
+        if (h(1, &v, nullptr) != 0) return LCPP_ERR_CUDA;
     return LCPP_OK;
 }
 

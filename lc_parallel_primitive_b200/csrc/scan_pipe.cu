@@ -6,7 +6,9 @@
 //    three 32 KiB shared-memory stages filled by TMA bulk copies
 //    (cp.async.bulk, this GPU's memory only, no multicast);
 //  * a CTA publishes the aggregate of its NEXT tile as soon as that tile's
-//    bulk load lands, before it resolves the look-back of its current tile.
+//    bulk load lands, before it resolves the look-back of its current tile;
+//    the next tile's warp sums and the current tile's warp totals cross one
+//    CTA barrier together (three barriers per tile in all).
 //    Partial descriptors therefore appear one tile ahead of the scan
 //    frontier, so a look-back never waits for another CTA's data to arrive
 //    (with one tile per CTA and no early publish, every look-back waits for
@@ -41,16 +43,17 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t s_bar[SP_STAGES];
     __shared__ unsigned int s_tile[SP_STAGES];
-    __shared__ T s_agg[SP_STAGES];
-    __shared__ T s_warp[SP_WARPS];
-    __shared__ T s_wex[SP_WARPS];
+    __shared__ T s_agg[SP_STAGES];      // aggregate of the tile held by each stage
+    __shared__ T s_wnext[SP_WARPS];     // warp sums of the next tile
+    __shared__ T s_wcur[SP_WARPS];      // warp totals of the current tile
+    __shared__ T s_wex[SP_WARPS];       // prefix of each warp's slice of the current tile
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint64_t full_tiles = n / SP_TILE;
     const uint32_t limit = g_spin_limit;
     const T c0 = carry_in ? *carry_in : init;
     const uint32_t woff = (uint32_t)warp * SP_WARP_ITEMS + lane * V;
-    uint32_t phase[SP_STAGES] = {};
+    uint32_t phase_bits = 0;  // bit st: parity of stage st's next phase
 
     auto issue = [&](unsigned int t, int st) {  // thread 0
         if (t < full_tiles) {
@@ -59,50 +62,73 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
             bulk_load(smem + st * SP_STAGE_BYTES, in + (uint64_t)t * SP_TILE, SP_STAGE_BYTES, &s_bar[st]);
         }
     };
-
-    // Make tile t's data available in stage st and publish its aggregate.
-    auto aggregate = [&](uint64_t t, int st) {
+    // Make stage st hold tile t for this thread's slice (the ragged last tile
+    // is copied slice by slice with identity fill, so no CTA barrier is needed).
+    auto wait_stage = [&](uint64_t t, int st) -> T* {
         T* buf = reinterpret_cast<T*>(smem + st * SP_STAGE_BYTES);
         if (t < full_tiles) {
-            if (!mbar_wait(&s_bar[st], phase[st], limit)) set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
-            phase[st] ^= 1;
-        } else {  // ragged last tile: guarded copy, zero fill
-            for (int i = tid; i < SP_TILE; i += SP_THREADS) {
-                const uint64_t g = t * SP_TILE + i;
-                buf[i] = g < n ? in[g] : Op::template identity<T>();
-            }
-            __syncthreads();
+            if (!mbar_wait(&s_bar[st], (phase_bits >> st) & 1u, limit)) set_error(LCPP_ERR_LOOKBACK_TIMEOUT);
+            phase_bits ^= 1u << st;
+        } else {
+#pragma unroll
+            for (int j = 0; j < SP_VECS; ++j)
+#pragma unroll
+                for (int k = 0; k < V; ++k) {
+                    const uint32_t i = woff + j * 32 * V + k;
+                    const uint64_t g = t * SP_TILE + i;
+                    buf[i] = g < n ? in[g] : Op::template identity<T>();
+                }
         }
-        T s = Op::template identity<T>();
+        return buf;
+    };
+    auto slice_sum = [&](const T* buf) -> T {  // warp-reduced sum of the warp's slice
+        T r = Op::template identity<T>();
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
             const uint4 q = *reinterpret_cast<const uint4*>(buf + woff + j * 32 * V);
             const T* e = reinterpret_cast<const T*>(&q);
-            if constexpr (V == 4)
-                s = Op::template apply<T>(s, Op::template apply<T>(Op::template apply<T>(e[0], e[1]), Op::template apply<T>(e[2], e[3])));
-            else
-                s = Op::template apply<T>(s, Op::template apply<T>(e[0], e[1]));
+#pragma unroll
+            for (int k = 0; k < V; ++k) r = Op::template apply<T>(r, e[k]);
         }
-        s = warp_reduce<Op>(s);
-        __syncthreads();  // earlier readers of s_warp are done
-        if (lane == 0) s_warp[warp] = s;
-        __syncthreads();
-        if (warp == 0) {
-            T a = lane < SP_WARPS ? s_warp[lane] : Op::template identity<T>();
-            a = warp_reduce<Op>(a);
-            if (lane == 0) {
-                s_agg[st] = a;
-                if (t == 0)
-                    desc.inclusive(0, Op::template apply<T>(c0, a));
-                else
-                    desc.partial((int64_t)t, a);
-            }
-        }
+        return warp_reduce<Op>(r);
+    };
+    auto tile_sum = [&](const T* ws) -> T {  // warp 0: sum of the SP_WARPS warp values
+        T a = lane < SP_WARPS ? ws[lane] : Op::template identity<T>();
+        return warp_reduce<Op>(a);
     };
 
-    // Scan tile t held in stage st (its aggregate already published).
-    auto scan_tile = [&](uint64_t t, int st) {
+    if (tid == 0) {
+        for (int i = 0; i < SP_STAGES; ++i) mbar_init(&s_bar[i], 1);
+        fence_mbar_init();
+        for (int i = 0; i < SP_STAGES; ++i) {
+            const unsigned int t = atomicAdd(ticket, 1u);
+            s_tile[i] = t;
+            issue(t, i);
+        }
+    }
+    __syncthreads();
+
+    uint64_t c = s_tile[0];
+    int st = 0;
+    if (c < num_tiles) {  // aggregate of the first tile
+        const T r = slice_sum(wait_stage(c, 0));
+        if (lane == 0) s_wnext[warp] = r;
+        __syncthreads();
+        if (warp == 0) {
+            const T a = tile_sum(s_wnext);
+            if (lane == 0) {
+                s_agg[0] = a;
+                if (c == 0) desc.inclusive(0, Op::template apply<T>(c0, a));
+                else desc.partial((int64_t)c, a);
+            }
+        }
+        __syncthreads();
+    }
+    while (c < num_tiles) {
+        const int nst = st + 1 == SP_STAGES ? 0 : st + 1;
+        const uint64_t nt = s_tile[nst];
         T* buf = reinterpret_cast<T*>(smem + st * SP_STAGE_BYTES);
+        // ---- local scan of the current tile; warp sums of the next one ---------
         T x[SP_VECS][V];
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
@@ -128,11 +154,22 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
             pre[j] = Op::template apply<T>(carry, excl);
             carry = Op::template apply<T>(carry, __shfl_sync(0xffffffffu, incl, 31));
         }
-        __syncthreads();  // aggregate()'s readers of s_warp are done
-        if (lane == 0) s_warp[warp] = carry;
+        if (lane == 0) s_wcur[warp] = carry;
+        if (nt < num_tiles) {
+            const T r = slice_sum(wait_stage(nt, nst));
+            if (lane == 0) s_wnext[warp] = r;
+        }
         __syncthreads();
+        // ---- warp 0: publish the next tile's aggregate, then resolve this one ---
         if (warp == 0) {
-            T incl = lane < SP_WARPS ? s_warp[lane] : Op::template identity<T>();
+            if (nt < num_tiles) {
+                const T a = tile_sum(s_wnext);
+                if (lane == 0) {
+                    s_agg[nst] = a;
+                    desc.partial((int64_t)nt, a);  // nt > c >= 0
+                }
+            }
+            T incl = lane < SP_WARPS ? s_wcur[lane] : Op::template identity<T>();
 #pragma unroll
             for (int o = 1; o < SP_WARPS; o <<= 1) {
                 const T y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -141,15 +178,16 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
             T wex = __shfl_up_sync(0xffffffffu, incl, 1);
             if (lane == 0) wex = Op::template identity<T>();
             T excl = c0;
-            if (t != 0) {
-                excl = lookback_warp<Op, T>(desc, (int64_t)t);
-                if (lane == 0) desc.inclusive((int64_t)t, Op::template apply<T>(excl, s_agg[st]));
+            if (c != 0) {
+                excl = lookback_warp<Op, T>(desc, (int64_t)c);
+                if (lane == 0) desc.inclusive((int64_t)c, Op::template apply<T>(excl, s_agg[st]));
             }
             if (lane < SP_WARPS) s_wex[lane] = Op::template apply<T>(excl, wex);
         }
         __syncthreads();
+        // ---- results into the stage (bulk store) or, for the ragged tile, out ---
         const T wbase = s_wex[warp];
-        const bool full = t < full_tiles;
+        const bool full = c < full_tiles;
 #pragma unroll
         for (int j = 0; j < SP_VECS; ++j) {
             const T b = Op::template apply<T>(wbase, pre[j]);
@@ -167,45 +205,23 @@ scan_pipe_kernel(const T* in, T* out, uint64_t n, uint64_t num_tiles, const T* c
             } else {
 #pragma unroll
                 for (int k = 0; k < V; ++k) {
-                    const uint64_t g = t * SP_TILE + woff + j * 32 * V + k;
+                    const uint64_t g = c * SP_TILE + woff + j * 32 * V + k;
                     if (g < n) out[g] = r[k];
                 }
             }
         }
         if (full) fence_proxy_async_smem();
         __syncthreads();
-        if (full && tid == 0) {
-            bulk_store(out + t * SP_TILE, buf, SP_STAGE_BYTES);
-            bulk_commit();
-        }
-    };
-
-    if (tid == 0) {
-        for (int i = 0; i < SP_STAGES; ++i) mbar_init(&s_bar[i], 1);
-        fence_mbar_init();
-        for (int i = 0; i < SP_STAGES; ++i) {
-            const unsigned int t = atomicAdd(ticket, 1u);
-            s_tile[i] = t;
-            issue(t, i);
-        }
-    }
-    __syncthreads();
-
-    uint64_t c = s_tile[0];
-    int st = 0;
-    if (c < num_tiles) aggregate(c, 0);
-    while (c < num_tiles) {
-        const int nst = st + 1 == SP_STAGES ? 0 : st + 1;
-        const uint64_t nt = s_tile[nst];
-        if (nt < num_tiles) aggregate(nt, nst);
-        scan_tile(c, st);
         if (tid == 0) {
+            if (full) {
+                bulk_store(out + c * SP_TILE, buf, SP_STAGE_BYTES);
+                bulk_commit();
+            }
             const unsigned int nnt = atomicAdd(ticket, 1u);
             s_tile[st] = nnt;
             bulk_wait_read_all();  // this stage's bulk store has read it
             issue(nnt, st);
         }
-        __syncthreads();
         c = nt;
         st = nst;
     }

@@ -1,2 +1,2 @@
-// Compilation unit of liblcpp_b200.so (relocatable device code): ScanByKey / ReduceByKey.
+// Compilation unit of liblcpp_b200.so: ScanByKey / ReduceByKey.
 #include "by_key.cu"

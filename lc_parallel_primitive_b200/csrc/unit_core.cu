@@ -1,4 +1,4 @@
-// Compilation unit of liblcpp_b200.so (relocatable device code): Reduce, ArgMin/ArgMax, segment reduce and the library-wide state.
+// Compilation unit of liblcpp_b200.so: Reduce, ArgMin/ArgMax, segment reduce and the library-wide state.
 #include "runtime.cu"
 #include "reduce.cu"
 #include "segment_reduce.cu"

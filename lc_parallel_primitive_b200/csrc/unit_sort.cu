@@ -1,3 +1,3 @@
-// Compilation unit of liblcpp_b200.so (relocatable device code): Radix sort and the multi-GPU primitives built on it.
+// Compilation unit of liblcpp_b200.so: Radix sort and the multi-GPU primitives built on it.
 #include "radix_sort.cu"
 #include "mg.cu"
