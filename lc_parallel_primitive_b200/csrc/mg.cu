@@ -19,18 +19,19 @@
 // shards in rank order):
 //   1. each rank takes 4096 evenly spaced samples of its shard, as extended
 //      keys (order-preserving key image, rank << 32 | index) weighted by the
-//      shard size; NCCL all-gathers them (and all-reduces the global key
-//      min/max: bits above the highest differing bit are equal in every key
-//      and need no sorting).  The gathered samples are sorted on the device
+//      shard size; NCCL all-gathers them.  The gathered samples are sorted on the device
 //      by this library's radix sort, and G-1 splitters are picked where the
 //      running weight crosses r/G.  Splitting on extended keys cuts runs of
 //      equal keys between ranks in input order, so every rank gets about
 //      n_total/G items whatever the key distribution.
 //   2. a bucket kernel gives every item its destination rank (number of
-//      splitters <= its extended key, one byte); one stable onesweep pass
-//      over those bytes groups the shard by destination.
-//   3. NCCL all-gather of the G bucket starts; this rank's send offsets and
-//      receive counts are copied to the host (the one synchronisation).
+//      splitters <= its extended key, one byte) and reduces the shard's key
+//      min/max; one stable onesweep pass over those bytes groups the shard
+//      by destination.
+//   3. one NCCL group all-gathers the G bucket starts and all-reduces the
+//      global key min/max (bits above the highest differing bit are equal in
+//      every key and need no sorting); this rank's send offsets and receive
+//      counts are copied to the host (the one synchronisation).
 //   4. grouped ncclSend/ncclRecv of keys and values; runs arrive in source
 //      rank order.
 //   5. local onesweep sort of the bits that differ, from the received runs
@@ -103,6 +104,20 @@ static const NcclApi& nccl() {
         if ((call) != cudaSuccess) return LCPP_ERR_CUDA;      \
     } while (0)
 
+// A non-blocking side stream per device (created on first use), on which the
+// sort copies this rank's own slice while NCCL moves the others.
+static cudaStream_t side_stream() {
+    static std::mutex mu;
+    static std::vector<cudaStream_t> streams;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> g(mu);
+    if ((size_t)dev >= streams.size()) streams.resize((size_t)dev + 1, nullptr);
+    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess)
+        streams[dev] = nullptr;
+    return streams[dev];
+}
+
 static bool nccl_type(int dtype, ncclDataType_t& t) {
     switch (dtype) {
         case LCPP_I32: t = ncclInt32; return true;
@@ -132,29 +147,6 @@ __global__ void mg_carry_kernel(const T* totals, int rank, T* carry) {
     T c = T(0);
     for (int h = 0; h < rank; ++h) c = OpSum::apply<T>(c, totals[h]);
     *carry = c;
-}
-
-// {min, ~max} of the ordered key image (min-reduction of both words gives the
-// global min and max).  Zero-length shards contribute the identity.
-template <typename KB, int KIND>
-__global__ void mg_minmax_kernel(const KB* keys, uint64_t n, unsigned long long* mm) {
-    unsigned long long lo = ~0ull, nhi = ~0ull;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
-        const unsigned long long o = (unsigned long long)ordered_bits<KB, KIND, false>(keys[i]);
-        lo = o < lo ? o : lo;
-        nhi = ~o < nhi ? ~o : nhi;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const unsigned long long a = __shfl_xor_sync(0xffffffffu, lo, off);
-        const unsigned long long b = __shfl_xor_sync(0xffffffffu, nhi, off);
-        lo = a < lo ? a : lo;
-        nhi = b < nhi ? b : nhi;
-    }
-    if ((threadIdx.x & 31) == 0) {
-        atomicMin(mm, lo);
-        atomicMin(mm + 1, nhi);
-    }
 }
 
 // Bits that still differ from the global {min, ~max}: info[1] = hb + 1,
@@ -238,8 +230,11 @@ __global__ void __launch_bounds__(1024) mg_pick_splitters_kernel(const uint64_t*
 // extended key, written as one byte per item.
 template <typename KB, int KIND>
 __global__ void mg_bucket_kernel(const KB* keys, uint64_t n, int me, const ulonglong2* split, int nsplit,
-                                 uint8_t* digits) {
+                                 uint8_t* digits, unsigned long long* mm) {
     __shared__ ulonglong2 s_split[256];
+    // {min, ~max} of the order-preserving key image (a min-reduction of both
+    // words gives the global min and max); empty shards leave the identity
+    unsigned long long kmin = ~0ull, nkmax = ~0ull;
     for (int i = threadIdx.x; i < nsplit; i += blockDim.x) s_split[i] = split[i];
     __syncthreads();
     const uint64_t rank_hi = (uint64_t)me << 32;
@@ -254,6 +249,19 @@ __global__ void mg_bucket_kernel(const KB* keys, uint64_t n, int me, const ulong
             if (le) lo = mid + 1; else hi = mid;
         }
         digits[i] = (uint8_t)lo;
+        kmin = o < kmin ? o : kmin;
+        nkmax = ~o < nkmax ? ~o : nkmax;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const unsigned long long x = __shfl_xor_sync(0xffffffffu, kmin, off);
+        const unsigned long long y = __shfl_xor_sync(0xffffffffu, nkmax, off);
+        kmin = x < kmin ? x : kmin;
+        nkmax = y < nkmax ? y : nkmax;
+    }
+    if ((threadIdx.x & 31) == 0) {
+        atomicMin(mm, kmin);
+        atomicMin(mm + 1, nkmax);
     }
 }
 
@@ -533,7 +541,7 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
     const DeviceInfo di = device_info();
     const unsigned grid = (unsigned)std::min<uint64_t>(ceil_div(n_local ? n_local : 1, 1024), (uint64_t)di.sms * 4);
     lcpp_status st;
-    // 1. global key range (bits that differ) and splitters from all ranks' samples
+    // 1. splitters from all ranks' samples
     {
         ProfScope ps("mg_splitters", s);
         MG_CUDA(cudaMemsetAsync(mm, 0xFF, 2 * sizeof(unsigned long long), s));
@@ -542,32 +550,26 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
             const KB* k = (const KB*)keys_in;
             const unsigned sg = (unsigned)ceil_div((uint64_t)MG_SAMPLES, 256);
             switch (kind) {
-                case 0: mg_minmax_kernel<KB, 0><<<grid, 1024, 0, s>>>(k, n_local, mm);
-                        mg_sample_kernel<KB, 0><<<sg, 256, 0, s>>>(k, n_local, me, skey + (size_t)me * MG_SAMPLES,
+                case 0: mg_sample_kernel<KB, 0><<<sg, 256, 0, s>>>(k, n_local, me, skey + (size_t)me * MG_SAMPLES,
                                                                    spos + (size_t)me * MG_SAMPLES, sw + (size_t)me * MG_SAMPLES, sidx, G);
                         break;
-                case 1: mg_minmax_kernel<KB, 1><<<grid, 1024, 0, s>>>(k, n_local, mm);
-                        mg_sample_kernel<KB, 1><<<sg, 256, 0, s>>>(k, n_local, me, skey + (size_t)me * MG_SAMPLES,
+                case 1: mg_sample_kernel<KB, 1><<<sg, 256, 0, s>>>(k, n_local, me, skey + (size_t)me * MG_SAMPLES,
                                                                    spos + (size_t)me * MG_SAMPLES, sw + (size_t)me * MG_SAMPLES, sidx, G);
                         break;
-                default: mg_minmax_kernel<KB, 2><<<grid, 1024, 0, s>>>(k, n_local, mm);
-                         mg_sample_kernel<KB, 2><<<sg, 256, 0, s>>>(k, n_local, me, skey + (size_t)me * MG_SAMPLES,
+                default: mg_sample_kernel<KB, 2><<<sg, 256, 0, s>>>(k, n_local, me, skey + (size_t)me * MG_SAMPLES,
                                                                     spos + (size_t)me * MG_SAMPLES, sw + (size_t)me * MG_SAMPLES, sidx, G);
                          break;
             }
-            count_launch(2);
+            count_launch();
             return check_launch();
         };
         st = ks == 4 ? go((uint32_t)0) : go((uint64_t)0);
         if (st != LCPP_OK) return st;
         MG_NCCL(A.GroupStart());
-        MG_NCCL(A.AllReduce(mm, mm + 2, 2, ncclUint64, ncclMin, c, s));
         MG_NCCL(A.AllGather(skey + (size_t)me * MG_SAMPLES, skey, MG_SAMPLES, ncclUint64, c, s));
         MG_NCCL(A.AllGather(spos + (size_t)me * MG_SAMPLES, spos, MG_SAMPLES, ncclUint64, c, s));
         MG_NCCL(A.AllGather(sw + (size_t)me * MG_SAMPLES, sw, MG_SAMPLES, ncclUint64, c, s));
         MG_NCCL(A.GroupEnd());
-        mg_range_bits_kernel<<<1, 1, 0, s>>>(mm + 2, info);
-        count_launch();
         // samples are gathered rank-major, positions ascending: a stable sort by
         // key leaves them in extended-key order
         st = rs_sort_impl(LCPP_U64, LCPP_U32, 0, skey, T + L.skey_sorted, sidx, T + L.order, (uint64_t)S, 0, 0,
@@ -588,9 +590,9 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
                 using KB = decltype(kb);
                 const KB* k = (const KB*)keys_in;
                 switch (kind) {
-                    case 0: mg_bucket_kernel<KB, 0><<<grid, 1024, 0, s>>>(k, n_local, me, split, G - 1, digits); break;
-                    case 1: mg_bucket_kernel<KB, 1><<<grid, 1024, 0, s>>>(k, n_local, me, split, G - 1, digits); break;
-                    default: mg_bucket_kernel<KB, 2><<<grid, 1024, 0, s>>>(k, n_local, me, split, G - 1, digits); break;
+                    case 0: mg_bucket_kernel<KB, 0><<<grid, 1024, 0, s>>>(k, n_local, me, split, G - 1, digits, mm); break;
+                    case 1: mg_bucket_kernel<KB, 1><<<grid, 1024, 0, s>>>(k, n_local, me, split, G - 1, digits, mm); break;
+                    default: mg_bucket_kernel<KB, 2><<<grid, 1024, 0, s>>>(k, n_local, me, split, G - 1, digits, mm); break;
                 }
                 count_launch();
                 return check_launch();
@@ -613,7 +615,12 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
         mg_pack_starts_kernel<<<1, 256, 0, s>>>((const uint32_t*)(T + L.sort), n_local, rows + (size_t)me * 257);
         count_launch();
         if ((st = check_launch()) != LCPP_OK) return st;
+        MG_NCCL(A.GroupStart());
         MG_NCCL(A.AllGather(rows + (size_t)me * 257, rows, 257, ncclUint64, c, s));
+        MG_NCCL(A.AllReduce(mm, mm + 2, 2, ncclUint64, ncclMin, c, s));
+        MG_NCCL(A.GroupEnd());
+        mg_range_bits_kernel<<<1, 1, 0, s>>>(mm + 2, info);
+        count_launch();
         mg_plan_kernel<<<1, 256, 0, s>>>(rows, G, me, info, (uint64_t*)(T + L.plan));
         count_launch();
         if ((st = check_launch()) != LCPP_OK) return st;
@@ -632,11 +639,22 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
     char* rv = vs ? T + L.recv_v : nullptr;
     {
         ProfScope ps("mg_exchange", s);
+        // this rank's own slice moves on a side stream, alongside the NCCL transfers
         const uint64_t self = so[me + 1] - so[me];
-        if (self) {
-            MG_CUDA(cudaMemcpyAsync(rk + ro[me] * ks, pk + so[me] * ks, self * ks, cudaMemcpyDeviceToDevice, s));
-            if (vs) MG_CUDA(cudaMemcpyAsync(rv + ro[me] * vs, pv + so[me] * vs, self * vs, cudaMemcpyDeviceToDevice, s));
+        cudaStream_t side = self ? side_stream() : nullptr;
+        cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+        if (side) {
+            MG_CUDA(cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming));
+            MG_CUDA(cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming));
+            MG_CUDA(cudaEventRecord(ev_in, s));
+            MG_CUDA(cudaStreamWaitEvent(side, ev_in, 0));
         }
+        if (self) {
+            cudaStream_t cs = side ? side : s;
+            MG_CUDA(cudaMemcpyAsync(rk + ro[me] * ks, pk + so[me] * ks, self * ks, cudaMemcpyDeviceToDevice, cs));
+            if (vs) MG_CUDA(cudaMemcpyAsync(rv + ro[me] * vs, pv + so[me] * vs, self * vs, cudaMemcpyDeviceToDevice, cs));
+        }
+        if (side) MG_CUDA(cudaEventRecord(ev_out, side));
         MG_NCCL(A.GroupStart());
         for (int p = 0; p < G; ++p) {
             if (p == me) continue;
@@ -651,6 +669,11 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
             }
         }
         MG_NCCL(A.GroupEnd());
+        if (side) {
+            MG_CUDA(cudaStreamWaitEvent(s, ev_out, 0));
+            cudaEventDestroy(ev_in);
+            cudaEventDestroy(ev_out);
+        }
     }
     // 5. local sort of the bits that still differ
     *n_out = n_recv;
