@@ -11,8 +11,8 @@
 // The communicator is the caller's ncclComm_t, passed as void*.
 //
 // Every entry point is asynchronous on the caller's stream except
-// lcpp_mg_sort, which waits once for the 2*G exchange counts (the sizes of
-// the NCCL send/receive calls must be known on the host).  Scratch comes from
+// lcpp_mg_sort, which waits for the exchange sizes (they must be known on the
+// host) and, on the IPC path, once more for the ranks' agreement on it.  Scratch comes from
 // the caller's temp buffer; nothing is allocated.
 //
 // Global sort, G ranks (ascending, stable over the concatenation of the
@@ -32,8 +32,11 @@
 //      global key min/max (bits above the highest differing bit are equal in
 //      every key and need no sorting); this rank's send offsets and receive
 //      counts are copied to the host (the one synchronisation).
-//   4. grouped ncclSend/ncclRecv of keys and values; runs arrive in source
-//      rank order.
+//   4. exchange of keys and values, runs landing in source rank order: each
+//      rank pulls its slices from the peers' shards by cudaMemcpyAsync over
+//      CUDA IPC mappings (copy engines, one stream per source; a one-word NCCL
+//      all-reduce then fences the shards), or, where a shard cannot be
+//      exported, grouped ncclSend/ncclRecv.
 //   5. local onesweep sort of the bits that differ, from the received runs
 //      into the caller's output.  Stable passes + rank-ordered runs keep
 //      equal keys in global input order.
@@ -44,6 +47,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 #include <mutex>
+#include <string>
 #include <vector>
 
 namespace lcpp {
@@ -104,18 +108,109 @@ static const NcclApi& nccl() {
         if ((call) != cudaSuccess) return LCPP_ERR_CUDA;      \
     } while (0)
 
-// A non-blocking side stream per device (created on first use), on which the
-// sort copies this rank's own slice while NCCL moves the others.
-static cudaStream_t side_stream() {
+// Non-blocking side streams per device (created on first use): stream 0
+// copies this rank's own slice, stream 1 + p pulls from peer p.
+struct SideStreams {
+    std::mutex mu;
+    std::vector<std::vector<cudaStream_t>> per_dev;
+};
+static SideStreams& side_streams() {
+    static SideStreams s;
+    return s;
+}
+static cudaStream_t side_stream(int i = 0) {
+    SideStreams& ss = side_streams();
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || i < 0) return nullptr;
+    std::lock_guard<std::mutex> g(ss.mu);
+    if ((size_t)dev >= ss.per_dev.size()) ss.per_dev.resize((size_t)dev + 1);
+    auto& v = ss.per_dev[dev];
+    if ((size_t)i >= v.size()) v.resize((size_t)i + 1, nullptr);
+    if (!v[i] && cudaStreamCreateWithFlags(&v[i], cudaStreamNonBlocking) != cudaSuccess) v[i] = nullptr;
+    return v[i];
+}
+// Wait for every side stream of the current device.
+static void sync_side_streams() {
+    SideStreams& ss = side_streams();
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return;
+    std::lock_guard<std::mutex> g(ss.mu);
+    if ((size_t)dev < ss.per_dev.size())
+        for (cudaStream_t st : ss.per_dev[dev])
+            if (st) cudaStreamSynchronize(st);
+}
+
+// ---------------------------------------------------------------------------
+// Exchange by CUDA IPC: every rank exports the allocation that holds its
+// partitioned shard (cudaIpcGetMemHandle on the allocation's base, found with
+// cuMemGetAddressRange), the handles travel with the bucket-start all-gather,
+// and each rank pulls its slices from the peers with cudaMemcpyAsync (copy
+// engines; no kernel reads peer memory).  Peer mappings are kept per device
+// and handle for the life of the process, so that repeated sorts from the
+// same buffers open each peer allocation once.
+// ---------------------------------------------------------------------------
+struct MgIpcRec {           // one per rank, all-gathered (12 x uint64)
+    cudaIpcMemHandle_t h;   // 64 bytes
+    uint64_t off_k, off_v;  // offsets of the partitioned keys / values from the allocation base
+    uint64_t ok;            // 1: exported
+};
+static_assert(sizeof(MgIpcRec) == 88, "MgIpcRec layout");
+constexpr size_t MG_IPC_REC_U64 = 12;  // 96 bytes on the wire
+
+using GetAddressRangeFn = int (*)(unsigned long long*, size_t*, unsigned long long);
+
+static bool alloc_base(const void* p, char** base) {
+    static GetAddressRangeFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (GetAddressRangeFn) nullptr;
+        return (GetAddressRangeFn)f;
+    }();
+    if (!fn) return false;
+    unsigned long long b = 0;
+    size_t sz = 0;
+    if (fn(&b, &sz, (unsigned long long)(uintptr_t)p) != 0) return false;
+    *base = (char*)(uintptr_t)b;
+    return true;
+}
+
+static bool mg_ipc_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("LCPP_MG_EXCHANGE");
+        return !(e && e[0] == 'n');  // LCPP_MG_EXCHANGE=nccl: NCCL send/recv only
+    }();
+    return on;
+}
+
+// Mapping of peer p's exported allocation in this process, kept per (device,
+// communicator, peer): a sort from the same buffers reuses it; when the peer
+// exports a different allocation, the old mapping is closed (after this
+// device's side streams, the only users of mappings, have drained), so that a
+// mapping never keeps a peer allocation alive after the peer has moved on.
+static char* open_peer(void* comm, int p, const cudaIpcMemHandle_t& h) {
+    struct Entry { int dev; void* comm; int peer; cudaIpcMemHandle_t h; char* ptr; };
     static std::mutex mu;
-    static std::vector<cudaStream_t> streams;
+    static std::vector<Entry> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
     std::lock_guard<std::mutex> g(mu);
-    if ((size_t)dev >= streams.size()) streams.resize((size_t)dev + 1, nullptr);
-    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess)
-        streams[dev] = nullptr;
-    return streams[dev];
+    for (auto it = cache.begin(); it != cache.end(); ++it) {
+        if (it->dev != dev || it->comm != comm || it->peer != p) continue;
+        if (memcmp(&it->h, &h, sizeof(h)) == 0) return it->ptr;
+        sync_side_streams();  // no copy from the old mapping is still in flight
+        cudaIpcCloseMemHandle(it->ptr);
+        cache.erase(it);
+        break;
+    }
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    cache.push_back(Entry{dev, comm, p, h, (char*)ptr});
+    return (char*)ptr;
 }
 
 static bool nccl_type(int dtype, ncclDataType_t& t) {
@@ -268,7 +363,8 @@ __global__ void mg_bucket_kernel(const KB* keys, uint64_t n, int me, const ulong
 // Plan of this rank from the all-gathered digit starts (G rows of 257:
 // starts[0..255] of the rank's partition pass, then its n).  Bucket p goes
 // to rank p.  out (uint64): [0..G] send offsets into this rank's partitioned
-// shard, [G+1..2G] receive counts per source rank, [2G+1] = info[1].
+// shard, [G+1..2G] receive counts per source rank, [2G+1] = info[1],
+// [2G+2..3G+1] where this rank's slice starts in each source's shard.
 __global__ void mg_plan_kernel(const uint64_t* rows, int G, int me, const uint32_t* info, uint64_t* out) {
     const uint64_t* mine = rows + (size_t)me * 257;
     for (int p = threadIdx.x; p <= G; p += blockDim.x) out[p] = p < 256 ? mine[p] : mine[256];
@@ -277,6 +373,7 @@ __global__ void mg_plan_kernel(const uint64_t* rows, int G, int me, const uint32
         const uint64_t hi = me + 1 < 256 ? row[me + 1] : row[256];
         out[G + 1 + p] = hi - row[me];
     }
+    for (int p = threadIdx.x; p < G; p += blockDim.x) out[2 * G + 2 + p] = rows[(size_t)p * 257 + me];
     if (threadIdx.x == 0) out[2 * G + 1] = info[1];
 }
 
@@ -292,7 +389,7 @@ __global__ void mg_pack_starts_kernel(const uint32_t* starts, uint64_t n, uint64
 // Sort temp layout
 // ---------------------------------------------------------------------------
 struct MgSortLayout {
-    size_t mm, info, rows, plan, skey, spos, sw, sidx, skey_sorted, order, split, digits;
+    size_t mm, info, rows, plan, ipc, skey, spos, sw, sidx, skey_sorted, order, split, digits;
     size_t part_k, part_v, recv_k, recv_v, sort, total;
 };
 
@@ -303,10 +400,11 @@ static MgSortLayout mg_sort_layout(int kdt, int vdt, uint64_t n_local, uint64_t 
     const size_t S = (size_t)G * MG_SAMPLES;
     size_t o = 0;
     auto take = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes, 256); return at; };
-    L.mm = take(4 * sizeof(unsigned long long));
+    L.mm = take(6 * sizeof(unsigned long long));  // local {min,~max}, global {min,~max}, agreement word
     L.info = take(2 * sizeof(uint32_t));
     L.rows = take((size_t)G * 257 * sizeof(uint64_t));
-    L.plan = take((size_t)(2 * G + 2) * sizeof(uint64_t));
+    L.plan = take((size_t)(3 * G + 2) * sizeof(uint64_t));
+    L.ipc = take((size_t)G * MG_IPC_REC_U64 * sizeof(uint64_t));
     uint64_t m = n_local;
     if (G > 1) {
         L.skey = take(S * 8);
@@ -607,9 +705,22 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
         }
     }
     // 3. all-gathered bucket starts -> exchange sizes -> host
-    std::vector<uint64_t> plan((size_t)2 * G + 2);
+    std::vector<uint64_t> plan((size_t)3 * G + 2);
+    std::vector<MgIpcRec> recs((size_t)G);
     uint64_t* rows = (uint64_t*)(T + L.rows);
+    uint64_t* ipc = (uint64_t*)(T + L.ipc);
     {
+        MgIpcRec mine{};
+        char* base = nullptr;
+        if (mg_ipc_enabled() && alloc_base(pk, &base) && cudaIpcGetMemHandle(&mine.h, base) == cudaSuccess) {
+            mine.off_k = (uint64_t)(pk - base);
+            mine.off_v = pv ? (uint64_t)(pv - base) : 0;
+            mine.ok = 1;
+        }
+        cudaGetLastError();  // an allocation that cannot be exported only selects the NCCL path
+        uint64_t wire[MG_IPC_REC_U64] = {};
+        memcpy(wire, &mine, sizeof(mine));
+        MG_CUDA(cudaMemcpyAsync(ipc + (size_t)me * MG_IPC_REC_U64, wire, sizeof(wire), cudaMemcpyHostToDevice, s));
         ProfScope ps("mg_plan", s);
         // the partition pass leaves its 256 digit starts at the start of its temp (bins of pass 0)
         mg_pack_starts_kernel<<<1, 256, 0, s>>>((const uint32_t*)(T + L.sort), n_local, rows + (size_t)me * 257);
@@ -618,6 +729,7 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
         MG_NCCL(A.GroupStart());
         MG_NCCL(A.AllGather(rows + (size_t)me * 257, rows, 257, ncclUint64, c, s));
         MG_NCCL(A.AllReduce(mm, mm + 2, 2, ncclUint64, ncclMin, c, s));
+        MG_NCCL(A.AllGather(ipc + (size_t)me * MG_IPC_REC_U64, ipc, MG_IPC_REC_U64, ncclUint64, c, s));
         MG_NCCL(A.GroupEnd());
         mg_range_bits_kernel<<<1, 1, 0, s>>>(mm + 2, info);
         count_launch();
@@ -625,8 +737,11 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
         count_launch();
         if ((st = check_launch()) != LCPP_OK) return st;
         MG_CUDA(cudaMemcpyAsync(plan.data(), T + L.plan, plan.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
+        std::vector<uint64_t> wires((size_t)G * MG_IPC_REC_U64);
+        MG_CUDA(cudaMemcpyAsync(wires.data(), ipc, wires.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
+        MG_CUDA(cudaStreamSynchronize(s));
+        for (int p = 0; p < G; ++p) memcpy(&recs[p], wires.data() + (size_t)p * MG_IPC_REC_U64, sizeof(MgIpcRec));
     }
-    MG_CUDA(cudaStreamSynchronize(s));
     const uint64_t* so = plan.data();
     const uint64_t* rc = plan.data() + G + 1;
     const int end_bit = (int)plan[2 * G + 1];
@@ -637,42 +752,83 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
     // 4. exchange (runs land in source-rank order)
     char* rk = T + L.recv_k;
     char* rv = vs ? T + L.recv_v : nullptr;
+    unsigned long long* agree = mm + 4;  // the path choice and the closing barrier
     {
         ProfScope ps("mg_exchange", s);
-        // this rank's own slice moves on a side stream, alongside the NCCL transfers
-        const uint64_t self = so[me + 1] - so[me];
-        cudaStream_t side = self ? side_stream() : nullptr;
-        cudaEvent_t ev_in = nullptr, ev_out = nullptr;
-        if (side) {
-            MG_CUDA(cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming));
-            MG_CUDA(cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming));
-            MG_CUDA(cudaEventRecord(ev_in, s));
-            MG_CUDA(cudaStreamWaitEvent(side, ev_in, 0));
+        // IPC pull when every rank exported its shard and mapped the peers it
+        // pulls from (decided together, so that no rank waits on a transfer its
+        // peer does not issue); NCCL send/recv otherwise.
+        bool use_ipc = true;
+        for (int p = 0; p < G; ++p) use_ipc = use_ipc && recs[p].ok == 1;
+        std::vector<char*> peer((size_t)G, nullptr);
+        if (use_ipc) {
+            unsigned long long mapped = 1;
+            for (int p = 0; p < G; ++p)
+                if (p != me && rc[p] && !(peer[p] = open_peer(comm, p, recs[p].h))) mapped = 0;
+            MG_CUDA(cudaMemcpyAsync(agree, &mapped, sizeof(mapped), cudaMemcpyHostToDevice, s));
+            MG_NCCL(A.AllReduce(agree, agree, 1, ncclUint64, ncclMin, c, s));
+            MG_CUDA(cudaMemcpyAsync(&mapped, agree, sizeof(mapped), cudaMemcpyDeviceToHost, s));
+            MG_CUDA(cudaStreamSynchronize(s));
+            use_ipc = mapped == 1;
         }
-        if (self) {
-            cudaStream_t cs = side ? side : s;
-            MG_CUDA(cudaMemcpyAsync(rk + ro[me] * ks, pk + so[me] * ks, self * ks, cudaMemcpyDeviceToDevice, cs));
-            if (vs) MG_CUDA(cudaMemcpyAsync(rv + ro[me] * vs, pv + so[me] * vs, self * vs, cudaMemcpyDeviceToDevice, cs));
-        }
-        if (side) MG_CUDA(cudaEventRecord(ev_out, side));
-        MG_NCCL(A.GroupStart());
-        for (int p = 0; p < G; ++p) {
-            if (p == me) continue;
-            const uint64_t sc = so[p + 1] - so[p];
-            if (sc) {
-                MG_NCCL(A.Send(pk + so[p] * ks, sc * ks, ncclUint8, p, c, s));
-                if (vs) MG_NCCL(A.Send(pv + so[p] * vs, sc * vs, ncclUint8, p, c, s));
+        if (use_ipc) {
+            // one side stream per source (this rank included), forked from and joined to s
+            std::vector<cudaEvent_t> ev((size_t)G + 1, nullptr);
+            for (auto& e : ev) MG_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            MG_CUDA(cudaEventRecord(ev[G], s));
+            for (int p = 0; p < G; ++p) {
+                if (!rc[p]) continue;
+                cudaStream_t sp = side_stream(1 + p);
+                if (!sp) return LCPP_ERR_CUDA;
+                MG_CUDA(cudaStreamWaitEvent(sp, ev[G], 0));
+                const char* src_k = p == me ? pk + so[me] * ks : peer[p] + recs[p].off_k + plan[2 * G + 2 + p] * ks;
+                MG_CUDA(cudaMemcpyAsync(rk + ro[p] * ks, src_k, rc[p] * ks, cudaMemcpyDeviceToDevice, sp));
+                if (vs) {
+                    const char* src_v = p == me ? pv + so[me] * vs : peer[p] + recs[p].off_v + plan[2 * G + 2 + p] * vs;
+                    MG_CUDA(cudaMemcpyAsync(rv + ro[p] * vs, src_v, rc[p] * vs, cudaMemcpyDeviceToDevice, sp));
+                }
+                MG_CUDA(cudaEventRecord(ev[p], sp));
+                MG_CUDA(cudaStreamWaitEvent(s, ev[p], 0));
             }
-            if (rc[p]) {
-                MG_NCCL(A.Recv(rk + ro[p] * ks, rc[p] * ks, ncclUint8, p, c, s));
-                if (vs) MG_NCCL(A.Recv(rv + ro[p] * vs, rc[p] * vs, ncclUint8, p, c, s));
+            for (auto& e : ev) cudaEventDestroy(e);
+            // every peer has finished reading this rank's shard before it is reused
+            MG_NCCL(A.AllReduce(agree, agree, 1, ncclUint64, ncclMin, c, s));
+        } else {
+            // this rank's own slice moves on a side stream, alongside the NCCL transfers
+            const uint64_t self = so[me + 1] - so[me];
+            cudaStream_t side = self ? side_stream() : nullptr;
+            cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+            if (side) {
+                MG_CUDA(cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming));
+                MG_CUDA(cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming));
+                MG_CUDA(cudaEventRecord(ev_in, s));
+                MG_CUDA(cudaStreamWaitEvent(side, ev_in, 0));
             }
-        }
-        MG_NCCL(A.GroupEnd());
-        if (side) {
-            MG_CUDA(cudaStreamWaitEvent(s, ev_out, 0));
-            cudaEventDestroy(ev_in);
-            cudaEventDestroy(ev_out);
+            if (self) {
+                cudaStream_t cs = side ? side : s;
+                MG_CUDA(cudaMemcpyAsync(rk + ro[me] * ks, pk + so[me] * ks, self * ks, cudaMemcpyDeviceToDevice, cs));
+                if (vs) MG_CUDA(cudaMemcpyAsync(rv + ro[me] * vs, pv + so[me] * vs, self * vs, cudaMemcpyDeviceToDevice, cs));
+            }
+            if (side) MG_CUDA(cudaEventRecord(ev_out, side));
+            MG_NCCL(A.GroupStart());
+            for (int p = 0; p < G; ++p) {
+                if (p == me) continue;
+                const uint64_t sc = so[p + 1] - so[p];
+                if (sc) {
+                    MG_NCCL(A.Send(pk + so[p] * ks, sc * ks, ncclUint8, p, c, s));
+                    if (vs) MG_NCCL(A.Send(pv + so[p] * vs, sc * vs, ncclUint8, p, c, s));
+                }
+                if (rc[p]) {
+                    MG_NCCL(A.Recv(rk + ro[p] * ks, rc[p] * ks, ncclUint8, p, c, s));
+                    if (vs) MG_NCCL(A.Recv(rv + ro[p] * vs, rc[p] * vs, ncclUint8, p, c, s));
+                }
+            }
+            MG_NCCL(A.GroupEnd());
+            if (side) {
+                MG_CUDA(cudaStreamWaitEvent(s, ev_out, 0));
+                cudaEventDestroy(ev_in);
+                cudaEventDestroy(ev_out);
+            }
         }
     }
     // 5. local sort of the bits that still differ

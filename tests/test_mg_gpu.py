@@ -90,7 +90,10 @@ def test_mg_rejects_bad_arguments(comm1):
     assert lib.lcpp_mg_reduce(0, L.U32, 1, 1, 10, 1, 16, None, None) in (L.ERR_NCCL, L.ERR_TEMP_TOO_SMALL)
 
 
-def test_mg_primitives_nccl(cuda):
+@pytest.mark.parametrize("exchange", ["ipc", "nccl"])
+def test_mg_primitives_nccl(cuda, exchange):
+    """2-4 ranks; the sort's exchange by CUDA IPC pulls (default) and by NCCL
+    send/recv (LCPP_MG_EXCHANGE=nccl)."""
     import torch
 
     ngpu = torch.cuda.device_count()
@@ -98,8 +101,10 @@ def test_mg_primitives_nccl(cuda):
         pytest.skip("needs 2 or more GPUs")
     n = min(ngpu, 4)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    if exchange == "nccl":
+        env["LCPP_MG_EXCHANGE"] = "nccl"
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
-                        "--master-addr", "127.0.0.1", "--master-port", "29533",
+                        "--master-addr", "127.0.0.1", "--master-port", str(29533 + (exchange == "nccl")),
                         str(ROOT / "tests" / "mg_gpu_worker.py")], capture_output=True, text=True, timeout=600,
                        env=env, cwd=str(ROOT))
     assert r.returncode == 0 and "MG_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
