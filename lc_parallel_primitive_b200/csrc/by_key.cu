@@ -458,10 +458,10 @@ by_key_pipe_kernel(const K* keys, const T* values, T* out_values, K* __restrict_
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t s_bar[BKP_STAGES];
     __shared__ unsigned int s_tile[BKP_STAGES];
-    __shared__ KPair<T> s_wagg[BK_WARPS];
+    __shared__ KPair<T> s_wagg[BKP_STAGES][BK_WARPS];  // indexed by stage: no barrier guards their reuse
     __shared__ KPair<T> s_wpre[BKP_STAGES][BK_WARPS];
     __shared__ KPair<T> s_tagg[BKP_STAGES];
-    __shared__ KPair<T> s_tpre;
+    __shared__ KPair<T> s_tpre[BKP_STAGES];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint64_t full_tiles = n / TILE;
@@ -548,11 +548,10 @@ by_key_pipe_kernel(const K* keys, const T* values, T* out_values, K* __restrict_
         }
         wex = kshfl_up(incl, 1);
         if (lane == 0) wex = kidentity<Op, T>();
-        __syncthreads();  // earlier readers of s_wagg are done
-        if (lane == 31) s_wagg[warp] = incl;
+        if (lane == 31) s_wagg[st][warp] = incl;
         __syncthreads();
         if (warp == 0) {
-            KPair<T> w = lane < BK_WARPS ? s_wagg[lane] : kidentity<Op, T>();
+            KPair<T> w = lane < BK_WARPS ? s_wagg[st][lane] : kidentity<Op, T>();
 #pragma unroll
             for (int o = 1; o < BK_WARPS; o <<= 1) {
                 const KPair<T> y = kshfl_up(w, o);
@@ -572,17 +571,17 @@ by_key_pipe_kernel(const K* keys, const T* values, T* out_values, K* __restrict_
     auto scan_tile = [&](uint64_t t, int st, uint32_t flags, const KPair<T>& wex) {
         const uint64_t base = t * TILE;
         const bool full = t < full_tiles;
-        __syncthreads();  // s_wpre / s_tagg of this stage visible; s_tpre free
+        // s_wpre / s_tagg of this stage were written one iteration earlier
         if (warp == 0) {
             KPair<T> tpre = kidentity<Op, T>();
             if (t != 0) {
                 tpre = bk_lookback<Op, T>(desc, (int64_t)t);
                 if (lane == 0) bk_publish(desc, (int64_t)t, 2u, kcombine<Op, T>(tpre, s_tagg[st]));
             }
-            if (lane == 0) s_tpre = tpre;
+            if (lane == 0) s_tpre[st] = tpre;
         }
         __syncthreads();
-        const KPair<T> tpre = s_tpre;
+        const KPair<T> tpre = s_tpre[st];
         KPair<T> run = kcombine<Op, T>(kcombine<Op, T>(tpre, s_wpre[st][warp]), wex);
         K k[ITEMS];
         T v[ITEMS];
@@ -670,18 +669,18 @@ by_key_pipe_kernel(const K* keys, const T* values, T* out_values, K* __restrict_
     while (c < num_tiles) {
         const int nst = st + 1 == BKP_STAGES ? 0 : st + 1;
         const uint64_t nt = s_tile[nst];
-        // The ticket for the stage this iteration frees is taken now by warp
-        // 1, so the atomic's round trip overlaps the two phases below.
-        const unsigned int pref = tid == 32 ? atomicAdd(ticket, 1u) : 0u;
+        // The ticket for the stage this iteration frees is taken now, so the
+        // atomic's round trip overlaps the two phases below.  The stage's new
+        // ticket is read two iterations later, past this iteration's barriers.
+        const unsigned int pref = tid == 0 ? atomicAdd(ticket, 1u) : 0u;
         if (nt < num_tiles) aggregate(nt, nst, fl_n, wx_n);
         scan_tile(c, st, fl_c, wx_c);
-        if (tid == 32) s_tile[st] = pref;
-        __syncthreads();
+        if (MODE == BK_REDUCE) __syncthreads();  // the compacted runs have left the stage
         if (tid == 0) {
+            s_tile[st] = pref;
             bulk_wait_read_all();  // this stage's bulk store has read it
-            issue(s_tile[st], st);
+            issue(pref, st);
         }
-        __syncthreads();
         c = nt;
         st = nst;
         fl_c = fl_n;

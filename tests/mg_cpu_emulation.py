@@ -90,7 +90,9 @@ def mg_sort(keys, vals):
     if G == 1:
         return oracle.radix_sort(keys, vals)
     o = ordered_image(keys)
-    # 1. global min / max of the image -> bits that still differ
+    # global min / max of the image -> bits that still differ (the library reduces
+    # it in its bucket kernel and all-reduces it with the bucket starts; the
+    # value is the same)
     lo = int(o.min()) if n else (1 << 64) - 1
     nhi = int(~o.max() & np.uint64((1 << 64) - 1)) if n else (1 << 64) - 1
     sign = np.uint64(1 << 63)
