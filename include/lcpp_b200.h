@@ -275,9 +275,12 @@ lcpp_status lcpp_mg_scan(int kind, int dtype, const void* in, void* out, uint64_
  * sampled from every shard (4096 samples per rank) on the extended key
  * (key, rank, index), so slices are near n_total / nranks whatever the key
  * distribution, duplicates included; a slice longer than capacity returns
- * LCPP_ERR_CAPACITY.  At most 256 ranks.  Equal keys keep
- * their global input order.  Waits once on `stream` (for the exchange
- * sizes); the rest is asynchronous.  n_local, capacity < 2^32. */
+ * LCPP_ERR_CAPACITY.  At most 256 ranks.  Slices move by CUDA IPC pulls (copy
+ * engines) when every rank's temp can be exported, else by NCCL send/recv
+ * (environment LCPP_MG_EXCHANGE=nccl forces it).  Equal keys keep
+ * their global input order.  Waits on `stream` for the exchange sizes (and
+ * once more for the ranks' agreement on the IPC path); the rest is
+ * asynchronous.  n_local, capacity < 2^32. */
 size_t      lcpp_mg_sort_temp_bytes(int key_dtype, int value_dtype, uint64_t n_local,
                                     uint64_t capacity, int nranks);
 lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* keys_in, const void* values_in,
