@@ -219,6 +219,7 @@ def main():
         from lc_parallel_primitive_b200 import multi_gpu as M
 
         comm = M.comm_for()
+        mg_nranks = comm.nranks  # ranks of the library's NCCL communicator (ncclCommCount)
         cap = M.default_capacity(n)
         mg_ko = torch.empty(cap, dtype=torch.uint32, device=dev)
         mg_vo = torch.empty(cap, dtype=torch.uint32, device=dev)
@@ -360,6 +361,7 @@ def main():
             "histogram_avg_ms": hist_avg_ms,
             "e2e": e2e,
             "gpu_launches": int(launches),
+            "comm_nranks": (mg_nranks if world > 1 else 1),
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "extras": extras,
