@@ -262,15 +262,16 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     unsigned char* p = smem + (size_t)TILE * sizeof(KB);
     VB* s_vals = reinterpret_cast<VB*>(p);
     if constexpr (HAS_V) p += (size_t)TILE * sizeof(VB);
-    uint32_t* s_wc = reinterpret_cast<uint32_t*>(p);          // [RS_WARPS][256]
-    uint32_t* s_gbase = s_wc + RS_WARPS * RS_DIGITS;         // [256]
+    // One word per (half-warp, digit): {lane mask of the half-warp : 16 | counter : 16}.
+    constexpr int RS_HALVES = 2 * RS_WARPS;
+    uint32_t* s_wc = reinterpret_cast<uint32_t*>(p);          // [RS_HALVES][256]
+    uint32_t* s_gbase = s_wc + RS_HALVES * RS_DIGITS;        // [256]
     uint32_t* s_misc = s_gbase + RS_DIGITS;                  // [0] tile id, [1..8] warp sums
-    uint32_t* s_wm = s_misc + 16;                            // [RS_WARPS][256] lane masks per digit
-    uint8_t* s_dig = reinterpret_cast<uint8_t*>(s_wm + RS_WARPS * RS_DIGITS);  // DIG: digit per tile slot
+    uint8_t* s_dig = reinterpret_cast<uint8_t*>(s_misc + 16);  // DIG: digit per tile slot
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) s_misc[0] = atomicAdd(a.ticket, 1u);
-    for (int i = tid; i < RS_WARPS * RS_DIGITS; i += THREADS) s_wc[i] = s_wm[i] = 0;
+    for (int i = tid; i < RS_HALVES * RS_DIGITS; i += THREADS) s_wc[i] = 0;
     // A pass in which one digit holds every item (skewed keys: e.g. the high
     // digits of keys with 8 bits of entropy) is the identity permutation.  The
     // flag is loaded now and looked at once the keys are in registers.
@@ -282,20 +283,23 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     const uint32_t num_valid = rem < (uint64_t)TILE ? (uint32_t)rem : (uint32_t)TILE;
 
     const KB* kin = reinterpret_cast<const KB*>(a.keys_in);
-    const uint32_t wbase = (uint32_t)warp * (ITEMS * 32);
+    // Each half-warp owns ITEMS * 16 consecutive items of the tile (item i of
+    // lane hl at hbase + i * 16 + hl) and ranks them with its own counters.
+    const uint32_t half = (uint32_t)lane >> 4, hl = (uint32_t)lane & 15;
+    const uint32_t hbase = (uint32_t)warp * (ITEMS * 32) + half * (ITEMS * 16) + hl;
 
     // ---- load (warp-striped) -------------------------------------------------
     KB key[ITEMS];
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
-        const uint32_t li = wbase + i * 32 + lane;
+        const uint32_t li = hbase + i * 16;
         key[i] = li < num_valid ? ldcs(kin + tile_base + li) : KB(0);
     }
     if (identity_pass) {  // keys back out where they came from, values copied; no rank, no look-back
         KB* kout0 = reinterpret_cast<KB*>(a.keys_out);
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
-            const uint32_t li = wbase + i * 32 + lane;
+            const uint32_t li = hbase + i * 16;
             if (li < num_valid) stcs(kout0 + tile_base + li, key[i]);
         }
         if constexpr (HAS_V) rs_copy_tile<VB>(a.vals_in, a.vals_out, tile_base, num_valid, tid, THREADS);
@@ -305,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     if constexpr (DIG) {
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
-            const uint32_t li = wbase + i * 32 + lane;
+            const uint32_t li = hbase + i * 16;
             dg[i] = li < num_valid ? (uint32_t)__ldcs(a.digits + tile_base + li) : (RS_DIGITS - 1);
         }
     }
@@ -330,11 +334,10 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     }
 
     // ---- early counts: per-warp digit histogram of the tile -------------------
-    uint32_t* wc = s_wc + warp * RS_DIGITS;
-    uint32_t* wm = s_wm + warp * RS_DIGITS;
+    uint32_t* wc = s_wc + (warp * 2 + half) * RS_DIGITS;
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
-        const uint32_t li = wbase + i * 32 + lane;
+        const uint32_t li = hbase + i * 16;
         const uint32_t d = digit_at(i, li);
         atomicAdd(wc + d, 1u);
     }
@@ -345,7 +348,7 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     uint32_t total = 0;
     if (tid < RS_DIGITS) {
 #pragma unroll
-        for (int w = 0; w < RS_WARPS; ++w) total += s_wc[w * RS_DIGITS + tid];
+        for (int w = 0; w < RS_HALVES; ++w) total += s_wc[w * RS_DIGITS + tid];
         if (tile == 0)
             lb_store(lb + tid, F::INCL | (W)(a.bins[tid] + total));
         else
@@ -364,10 +367,10 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     if (tid < RS_DIGITS) {
         for (int w = 0; w < warp; ++w) off += s_misc[1 + w];
         off += incl - total;
-        // each warp's counter starts at the tile position of its first key of d
+        // each half-warp's counter starts at the tile position of its first key of d
         uint32_t run = off;
 #pragma unroll
-        for (int w = 0; w < RS_WARPS; ++w) {
+        for (int w = 0; w < RS_HALVES; ++w) {
             const uint32_t c = s_wc[w * RS_DIGITS + tid];
             s_wc[w * RS_DIGITS + tid] = run;
             run += c;
@@ -418,29 +421,24 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
     }
 
     // ---- stable rank: keys straight to their tile position in shared memory --
-    const uint32_t lt = lanemask_lt();
+    const uint32_t lt = (1u << hl) - 1u;
     uint32_t pos[ITEMS];
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
-        const uint32_t li = wbase + i * 32 + lane;
+        const uint32_t li = hbase + i * 16;
         const uint32_t d = digit_at(i, li);
-        // Lanes holding the same digit: each lane sets its bit in the warp's
-        // mask word for its digit, reads the word back, and the highest lane
-        // of the group advances the warp's running position and clears the word.
-        atomicOr(wm + d, 1u << lane);
+        // Lanes of a half-warp holding the same digit set their bits in the
+        // mask half of the word, read the word back (mask of peers and the
+        // running position), and the highest peer writes the advanced
+        // position with the mask cleared: three shared-memory accesses per key.
+        atomicOr(wc + d, 1u << (16 + hl));
         __syncwarp();
-        const uint32_t peers = wm[d];
-        const int leader = 31 - __clz(peers);
+        const uint32_t v = wc[d];
+        const uint32_t peers = v >> 16;
         __syncwarp();
-        uint32_t old = 0;
-        if (lane == leader) {
-            old = wc[d];
-            wc[d] = old + __popc(peers);
-            wm[d] = 0;
-        }
-        old = __shfl_sync(0xffffffffu, old, leader);
+        pos[i] = (v & 0xFFFFu) + __popc(peers & lt);
+        if ((peers >> hl) == 1u) wc[d] = (v & 0xFFFFu) + __popc(peers);
         __syncwarp();
-        pos[i] = old + __popc(peers & lt);
         s_keys[pos[i]] = key[i];
         if constexpr (DIG) s_dig[pos[i]] = (uint8_t)d;
     }
@@ -452,18 +450,18 @@ __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(Rs
             cp_async_wait_all();
             __syncthreads();  // every thread's chunks have landed
 #pragma unroll
-            for (int i = 0; i < ITEMS; ++i) val[i] = s_vals[wbase + i * 32 + lane];
+            for (int i = 0; i < ITEMS; ++i) val[i] = s_vals[hbase + i * 16];
             __syncthreads();  // staging fully read before it is overwritten
         } else {
 #pragma unroll
             for (int i = 0; i < ITEMS; ++i) {
-                const uint32_t li = wbase + i * 32 + lane;
+                const uint32_t li = hbase + i * 16;
                 if (li < num_valid) val[i] = ldcs(vin + tile_base + li);
             }
         }
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
-            const uint32_t li = wbase + i * 32 + lane;
+            const uint32_t li = hbase + i * 16;
             if (li < num_valid) s_vals[pos[i]] = val[i];
         }
     }
