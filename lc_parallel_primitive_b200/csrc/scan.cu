@@ -56,9 +56,13 @@ template <> __device__ __forceinline__ int32_t from_bits<int32_t>(uint32_t b) { 
 //    and read with relaxed device-scope accesses, so value and status are
 //    always seen together (the reference writes them as separate volatile
 //    stores with no fence, single_pass_scan_operator.h:81-93).
-//  * 8-byte values: a status word per tile plus an aggregate slot and an
-//    inclusive slot; the value is stored before a release store of the
-//    status, and read after an acquire load of it.
+//  * 8-byte values: two 64-bit words per tile, {status:32 | low half:32} and
+//    {status:32 | high half:32}, written and read with relaxed device-scope
+//    accesses (the two loads are independent, so both are in flight at once).
+//    Each status is written once per tile with one value, so when both words
+//    show the same status their halves belong to the same value; a reader
+//    that sees different statuses (a write in between) treats the tile as not
+//    yet published and loads it again.
 template <typename T, bool WIDE = (sizeof(T) == 8)>
 struct ScanDesc;
 
@@ -76,38 +80,27 @@ struct ScanDesc<T, false> {
     }
 };
 
-__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 template <typename T>
 struct ScanDesc<T, true> {
-    uint32_t* status;
-    T* agg;
-    T* incl;
-    static size_t bytes(uint64_t tiles) { return align_up(tiles * 4, 256) + 2 * align_up(tiles * 8, 256); }
-    static ScanDesc carve(void* p, uint64_t tiles) {
-        char* c = (char*)p;
-        return ScanDesc{(uint32_t*)c, (T*)(c + align_up(tiles * 4, 256)),
-                        (T*)(c + align_up(tiles * 4, 256) + align_up(tiles * 8, 256))};
+    uint64_t* w;  // [tiles][2]
+    static size_t bytes(uint64_t tiles) { return align_up(tiles * 16, 256); }
+    static ScanDesc carve(void* p, uint64_t) { return ScanDesc{(uint64_t*)p}; }
+    __device__ __forceinline__ void put(int64_t t, uint64_t st, T v) const {
+        uint64_t b;
+        memcpy(&b, &v, 8);
+        st_relaxed_u64(w + 2 * t, st | (b & 0xFFFFFFFFull));
+        st_relaxed_u64(w + 2 * t + 1, st | (b >> 32));
     }
-    __device__ __forceinline__ void partial(int64_t t, T v) const {
-        st_relaxed_u64(reinterpret_cast<uint64_t*>(agg + t), __builtin_bit_cast(uint64_t, v));
-        st_release_u32(status + t, 1u);
-    }
-    __device__ __forceinline__ void inclusive(int64_t t, T v) const {
-        st_relaxed_u64(reinterpret_cast<uint64_t*>(incl + t), __builtin_bit_cast(uint64_t, v));
-        st_release_u32(status + t, 2u);
-    }
+    __device__ __forceinline__ void partial(int64_t t, T v) const { put(t, ST_PARTIAL, v); }
+    __device__ __forceinline__ void inclusive(int64_t t, T v) const { put(t, ST_INCLUSIVE, v); }
     __device__ __forceinline__ uint32_t load(int64_t t, T& v) const {
-        const uint32_t st = ld_acquire_u32(status + t);
-        if (st) v = __builtin_bit_cast(T, ld_relaxed_u64(reinterpret_cast<const uint64_t*>(st == 1 ? agg + t : incl + t)));
-        return st;
+        const uint64_t d0 = ld_relaxed_u64(w + 2 * t);
+        const uint64_t d1 = ld_relaxed_u64(w + 2 * t + 1);
+        const uint32_t s0 = (uint32_t)(d0 >> 32);
+        if (s0 != (uint32_t)(d1 >> 32)) return 0u;  // halves of different writes: not yet published
+        const uint64_t b = (d1 << 32) | (d0 & 0xFFFFFFFFull);
+        memcpy(&v, &b, 8);
+        return s0;
     }
 };
 
