@@ -109,7 +109,7 @@ static const NcclApi& nccl() {
     } while (0)
 
 // Non-blocking side streams per device (created on first use): stream 0
-// copies this rank's own slice, stream 1 + p pulls from peer p.
+// copies this rank's own slice, streams 1 + p K .. p K + K pull from peer p.
 struct SideStreams {
     std::mutex mu;
     std::vector<std::vector<cudaStream_t>> per_dev;
@@ -174,6 +174,16 @@ static bool alloc_base(const void* p, char** base) {
     if (fn(&b, &sz, (unsigned long long)(uintptr_t)p) != 0) return false;
     *base = (char*)(uintptr_t)b;
     return true;
+}
+
+// Copy streams per source rank of the IPC exchange (LCPP_MG_PULL_STREAMS, 1..16).
+static int mg_pull_streams() {
+    static const int k = [] {
+        const char* e = getenv("LCPP_MG_PULL_STREAMS");
+        const int v = e ? atoi(e) : 4;
+        return v < 1 ? 1 : (v > 16 ? 16 : v);
+    }();
+    return k;
 }
 
 static bool mg_ipc_enabled() {
@@ -772,23 +782,34 @@ extern "C" lcpp_status lcpp_mg_sort(int key_dtype, int value_dtype, const void* 
             use_ipc = mapped == 1;
         }
         if (use_ipc) {
-            // one side stream per source (this rank included), forked from and joined to s
-            std::vector<cudaEvent_t> ev((size_t)G + 1, nullptr);
+            // K side streams per source (this rank included), forked from and
+            // joined to s: each carries 1/K of the slice, so that several copy
+            // engines pull from every source at once.
+            const int K = mg_pull_streams();
+            std::vector<cudaEvent_t> ev((size_t)G * K + 1, nullptr);
             for (auto& e : ev) MG_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-            MG_CUDA(cudaEventRecord(ev[G], s));
+            MG_CUDA(cudaEventRecord(ev[(size_t)G * K], s));
             for (int p = 0; p < G; ++p) {
                 if (!rc[p]) continue;
-                cudaStream_t sp = side_stream(1 + p);
-                if (!sp) return LCPP_ERR_CUDA;
-                MG_CUDA(cudaStreamWaitEvent(sp, ev[G], 0));
                 const char* src_k = p == me ? pk + so[me] * ks : peer[p] + recs[p].off_k + plan[2 * G + 2 + p] * ks;
-                MG_CUDA(cudaMemcpyAsync(rk + ro[p] * ks, src_k, rc[p] * ks, cudaMemcpyDeviceToDevice, sp));
-                if (vs) {
-                    const char* src_v = p == me ? pv + so[me] * vs : peer[p] + recs[p].off_v + plan[2 * G + 2 + p] * vs;
-                    MG_CUDA(cudaMemcpyAsync(rv + ro[p] * vs, src_v, rc[p] * vs, cudaMemcpyDeviceToDevice, sp));
+                const char* src_v = !vs ? nullptr
+                                  : p == me ? pv + so[me] * vs
+                                            : peer[p] + recs[p].off_v + plan[2 * G + 2 + p] * vs;
+                const uint64_t per = ceil_div(rc[p], (uint64_t)K);
+                for (int j = 0; j < K; ++j) {
+                    const uint64_t b0 = (uint64_t)j * per;
+                    if (b0 >= rc[p]) break;
+                    const uint64_t cnt = std::min<uint64_t>(per, rc[p] - b0);
+                    cudaStream_t sp = side_stream(1 + p * K + j);
+                    if (!sp) return LCPP_ERR_CUDA;
+                    MG_CUDA(cudaStreamWaitEvent(sp, ev[(size_t)G * K], 0));
+                    MG_CUDA(cudaMemcpyAsync(rk + (ro[p] + b0) * ks, src_k + b0 * ks, cnt * ks, cudaMemcpyDeviceToDevice, sp));
+                    if (vs)
+                        MG_CUDA(cudaMemcpyAsync(rv + (ro[p] + b0) * vs, src_v + b0 * vs, cnt * vs,
+                                                cudaMemcpyDeviceToDevice, sp));
+                    MG_CUDA(cudaEventRecord(ev[(size_t)p * K + j], sp));
+                    MG_CUDA(cudaStreamWaitEvent(s, ev[(size_t)p * K + j], 0));
                 }
-                MG_CUDA(cudaEventRecord(ev[p], sp));
-                MG_CUDA(cudaStreamWaitEvent(s, ev[p], 0));
             }
             for (auto& e : ev) cudaEventDestroy(e);
             // every peer has finished reading this rank's shard before it is reused
