@@ -36,7 +36,10 @@ namespace lcpp {
 
 constexpr int RS_BITS = 8;
 constexpr int RS_DIGITS = 1 << RS_BITS;
-constexpr int RS_THREADS = 512;
+#ifndef LCPP_RS_THREADS_CT
+#define LCPP_RS_THREADS_CT 512
+#endif
+constexpr int RS_THREADS = LCPP_RS_THREADS_CT;
 constexpr int RS_WARPS = RS_THREADS / 32;
 constexpr int RS_MAX_PASSES = 8;
 constexpr int RS_LB_WINDOW = 8;  // predecessor words loaded per look-back step
@@ -495,20 +498,11 @@ struct RsLayout {
     size_t bins_off, ticket_off, lb_off, keys_off, vals_off, total, zero_bytes;
 };
 
-// CTA size of the onesweep kernel (tuning knob LCPP_RS_THREADS = 256 | 512).
-static int rs_threads() {
-    static const int t = [] {
-        const char* e = getenv("LCPP_RS_THREADS");
-        return (e && atoi(e) == 256) ? 256 : RS_THREADS;
-    }();
-    return t;
-}
-
 static RsLayout rs_layout(size_t ksize, size_t vsize, uint64_t n, uint32_t passes) {
     RsLayout L{};
     const int items = ksize == 4 ? RsItems<uint32_t>::value : RsItems<uint64_t>::value;
     L.passes = passes;
-    L.tiles = ceil_div(n ? n : 1, (uint64_t)rs_threads() * items);
+    L.tiles = ceil_div(n ? n : 1, (uint64_t)RS_THREADS * items);
     L.lb_word = n < (1ull << 30) ? 4 : 8;
     L.bins_off = 0;
     L.ticket_off = align_up(RS_MAX_PASSES * RS_DIGITS * 4, 256);
@@ -562,7 +556,7 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
         rs_bins_scan_kernel<<<L.passes, RS_DIGITS, 0, s>>>(bins, n, tickets + RS_MAX_PASSES); }
         count_launch(2);
     }
-    const int threads = digits ? RS_THREADS : rs_threads();
+    const int threads = RS_THREADS;
     size_t smem;
     void (*kern)(RsPass);
     if (digits) {  // one pass over precomputed digits (only unsigned ascending instantiations)
@@ -573,9 +567,8 @@ static lcpp_status rs_run(const RsLayout& L, const void* keys_in, void* keys_out
             return LCPP_ERR_INVALID_ARG;
         }
     } else {
-        smem = threads == 256 ? rs_smem_bytes<KB, VB, 256>() : rs_smem_bytes<KB, VB, RS_THREADS>();
-        kern = threads == 256 ? rs_onesweep_kernel<KB, VB, W, KIND, DESC, 256>
-                              : rs_onesweep_kernel<KB, VB, W, KIND, DESC, RS_THREADS>;
+        smem = rs_smem_bytes<KB, VB, RS_THREADS>();
+        kern = rs_onesweep_kernel<KB, VB, W, KIND, DESC, RS_THREADS>;
     }
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return LCPP_ERR_CUDA;
