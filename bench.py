@@ -39,7 +39,7 @@ METRIC = "Onesweep sort Gkeys/s; scan/reduce HBM GB/s (% of ~8 TB/s) at 1/2/4/8 
 UNIT = "Gkeys/s"
 # DRAM bytes per pair per onesweep launch from the committed ncu capture
 # (profiles/), or None before one exists.
-TRAFFIC_PER_PAIR_PASS = 15.25  # DRAM bytes per pair per pass, 2^26 capture in profiles/dram_traffic_sort_scan_2p26.md
+TRAFFIC_PER_PAIR_PASS = 4.27e9 / 2**28  # DRAM bytes per pair per pass, 2^28 capture in profiles/sort_pairs_u32_2p28_launches.md
 
 
 def load_peaks():
@@ -352,9 +352,9 @@ def main():
                          "achieved": os_achieved, "peak": peak, "unit": "GB/s", "frac": os_achieved / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                          "traffic": TRAFFIC_PER_PAIR_PASS * n if TRAFFIC_PER_PAIR_PASS else None,
-                         "traffic_source": "ncu dram__bytes_read+write of one onesweep launch at 2^26 pairs "
-                                           "(profiles/dram_traffic_sort_scan_2p26.md), 15.25 B per pair, scaled "
-                                           "to 2^28 pairs by the pair count",
+                         "traffic_source": "ncu dram__bytes_read+write of one onesweep launch at 2^28 pairs "
+                                           "(profiles/sort_pairs_u32_2p28_launches.md), 15.9 B per pair; scaled "
+                                           "by the pair count when n differs",
                          "avg_launch_ms": os_avg_ms, "bytes_per_launch": os_bytes,
                          "whole_sort_frac": (68 * n / (ms * 1e-3) / 1e9) / peak},
             "kernels": {k: {"launches": c, "total_ms": t} for k, (c, t) in prof.items()},
