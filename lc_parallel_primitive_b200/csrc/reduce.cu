@@ -106,7 +106,15 @@ reduce_kernel(const T* __restrict__ in, uint64_t n, T* __restrict__ partials,
 #pragma unroll
         for (int u = 0; u < REDUCE_UNROLL; ++u) acc = fold_vec<Op, T, VEC, Xf>(acc, q[u], k);
     }
-    for (; i < nvec; i += gstride) acc = fold_vec<Op, T, VEC, Xf>(acc, ld_stream(vin + i), k);
+    if (i < nvec) {  // the last partial round: its loads are issued together, not one round trip each
+        uint4 q[REDUCE_UNROLL - 1];
+#pragma unroll
+        for (int u = 0; u < REDUCE_UNROLL - 1; ++u)
+            if (i + u * gstride < nvec) q[u] = ld_stream(vin + i + u * gstride);
+#pragma unroll
+        for (int u = 0; u < REDUCE_UNROLL - 1; ++u)
+            if (i + u * gstride < nvec) acc = fold_vec<Op, T, VEC, Xf>(acc, q[u], k);
+    }
     const uint64_t tail0 = head + nvec * VEC;
     if (tail0 + gtid < n) acc = Op::template apply<T>(acc, Xf::template apply<T>(in[tail0 + gtid], k));
 
