@@ -93,26 +93,23 @@ __device__ __forceinline__ KPair<T> kshfl(const KPair<T>& p, int src) {
     return r;
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Two descriptor forms.  Packed (4-byte values, n < 2^30): one 64-bit word
-// per tile {status:2 | count:30 | value:32} written and read with relaxed
-// device-scope accesses, so no fence is needed.  Otherwise: a status word per
-// tile plus separate partial / inclusive pair slots, slot before status with
-// release / acquire ordering.
+// Two descriptor forms, both written and read with relaxed device-scope
+// accesses only (no fences).  Packed (4-byte values, n < 2^30): one 64-bit
+// word per tile {status:2 | count:30 | value:32}.  Split (otherwise): WPT
+// 64-bit words per tile, {status:32 | count:32}, {status:32 | value bits
+// 0..31} and, for 8-byte values, {status:32 | value bits 32..63}.  Each
+// status is written once per tile with one pair, so when every word of a
+// tile shows the same status the words belong to the same pair; a reader
+// that sees different statuses (a write in between) polls the tile again.
 template <typename T>
 struct BkDesc {
-    uint64_t* packed;     // non-null: packed form
-    uint32_t* status;     // 0 = not ready, 1 = partial, 2 = inclusive
-    KPair<T>* partial;
-    KPair<T>* inclusive;
+    uint64_t* packed;  // non-null: packed form
+    uint64_t* split;   // otherwise: [tiles][WPT]
+    static constexpr int WPT = sizeof(T) == 8 ? 3 : 2;
+};
+
+struct BkRaw {
+    uint64_t w[3];
 };
 
 template <typename T>
@@ -138,32 +135,45 @@ __device__ __forceinline__ void bk_publish(const BkDesc<T>& d, int64_t tile, uin
             return;
         }
     }
-    KPair<T>* slot = (st == 2 ? d.inclusive : d.partial) + tile;
-    __stcg(&slot->count, p.count);
-    __stcg(&slot->value, p.value);
-    st_release_u32(d.status + tile, st);
+    uint64_t* w = d.split + tile * BkDesc<T>::WPT;
+    const uint64_t hi = (uint64_t)st << 32;
+    uint64_t b = 0;
+    memcpy(&b, &p.value, sizeof(T));
+    st_relaxed_u64(w, hi | p.count);
+    st_relaxed_u64(w + 1, hi | (b & 0xFFFFFFFFull));
+    if constexpr (sizeof(T) == 8) st_relaxed_u64(w + 2, hi | (b >> 32));
 }
 
-// Status of tile p (0 = not ready), and its pair once ready.
+// Status of tile p (0 = not ready), and its raw words once ready.
 template <typename T>
-__device__ __forceinline__ uint32_t bk_poll(const BkDesc<T>& d, int64_t p, uint64_t& word) {
+__device__ __forceinline__ uint32_t bk_poll(const BkDesc<T>& d, int64_t p, BkRaw& r) {
     if constexpr (sizeof(T) == 4) {
         if (d.packed) {
-            word = ld_relaxed_u64(d.packed + p);
-            return (uint32_t)(word >> 62);
+            r.w[0] = ld_relaxed_u64(d.packed + p);
+            return (uint32_t)(r.w[0] >> 62);
         }
     }
-    return ld_acquire_u32(d.status + p);
+    const uint64_t* w = d.split + p * BkDesc<T>::WPT;
+    r.w[0] = ld_relaxed_u64(w);
+    r.w[1] = ld_relaxed_u64(w + 1);
+    const uint32_t st = (uint32_t)(r.w[0] >> 32);
+    bool same = (uint32_t)(r.w[1] >> 32) == st;
+    if constexpr (sizeof(T) == 8) {
+        r.w[2] = ld_relaxed_u64(w + 2);
+        same = same && (uint32_t)(r.w[2] >> 32) == st;
+    }
+    return same ? st : 0u;
 }
 template <typename T>
-__device__ __forceinline__ KPair<T> bk_fetch(const BkDesc<T>& d, int64_t p, uint32_t st, uint64_t word) {
+__device__ __forceinline__ KPair<T> bk_fetch(const BkDesc<T>& d, int64_t, uint32_t, const BkRaw& r) {
     if constexpr (sizeof(T) == 4) {
-        if (d.packed) return bk_unpack<T>(word);
+        if (d.packed) return bk_unpack<T>(r.w[0]);
     }
     KPair<T> v;
-    const KPair<T>* slot = (st == 2 ? d.inclusive : d.partial) + p;
-    v.count = __ldcg(&slot->count);
-    v.value = __ldcg(&slot->value);
+    v.count = (uint32_t)r.w[0];
+    uint64_t b = r.w[1] & 0xFFFFFFFFull;
+    if constexpr (sizeof(T) == 8) b |= r.w[2] << 32;
+    memcpy(&v.value, &b, sizeof(T));
     return v;
 }
 
@@ -178,7 +188,7 @@ __device__ KPair<T> bk_lookback(const BkDesc<T>& d, int64_t tile) {
     int64_t p = tile - 1 - lane;
     uint32_t spins = 0;
     while (true) {
-        uint64_t word = 0;
+        BkRaw word{};
         uint32_t st = p >= 0 ? bk_poll(d, p, word) : 2u;
         while (__any_sync(0xffffffffu, st == 0)) {
             if (++spins > limit) {
@@ -701,11 +711,11 @@ static lcpp_status bk_launch(const void* keys, const void* values, void* out_val
     unsigned int* ticket = (unsigned int*)temp;
     BkDesc<T> d;
     const bool packed = sizeof(T) == 4 && n < (1ull << 30);
-    d.status = (uint32_t*)((char*)temp + BK_HDR);
-    d.packed = packed ? (uint64_t*)d.status : nullptr;
-    d.partial = (KPair<T>*)((char*)d.status + align_up(tiles * 8, 256));
-    d.inclusive = (KPair<T>*)((char*)d.partial + align_up(tiles * sizeof(KPair<T>), 256));
-    if (cudaMemsetAsync(temp, 0, BK_HDR + tiles * (packed ? 8 : 4), s) != cudaSuccess) return LCPP_ERR_CUDA;
+    uint64_t* words = (uint64_t*)((char*)temp + BK_HDR);
+    d.packed = packed ? words : nullptr;
+    d.split = packed ? nullptr : words;
+    if (cudaMemsetAsync(temp, 0, BK_HDR + tiles * 8 * (packed ? 1 : BkDesc<T>::WPT), s) != cudaSuccess)
+        return LCPP_ERR_CUDA;
     const bool vec = ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values) |
                        (MODE == BK_REDUCE ? 0 : reinterpret_cast<uintptr_t>(out_values))) & 15) == 0;
     ProfScope ps(MODE == BK_REDUCE ? "reduce_by_key" : "scan_by_key", s);
@@ -737,8 +747,7 @@ static size_t bk_temp_bytes(int key_dtype, int value_dtype, uint64_t n) {
     const size_t ks = lcpp_dtype_size(key_dtype), vs = lcpp_dtype_size(value_dtype);
     if (!ks || !vs) return 0;
     const uint64_t tiles = ceil_div(n ? n : 1, BK_DESC_TILE);
-    const size_t pair = vs == 8 ? 16 : 8;
-    return BK_HDR + align_up(tiles * 8, 256) + 2 * align_up(tiles * pair, 256);
+    return BK_HDR + align_up(tiles * 8 * (vs == 8 ? 3 : 2), 256);  // packed form: 1 word per tile
 }
 
 // Key dispatch: integer keys compare by bits, float keys by value.
