@@ -19,6 +19,7 @@
 // Each segment is reduced by exactly one warp or one CTA in a fixed order, so
 // float results do not depend on scheduling.
 #include "common.cuh"
+#include <algorithm>
 
 namespace lcpp {
 
@@ -207,12 +208,31 @@ segf_partition_kernel(const uint32_t* __restrict__ begin, const uint32_t* __rest
     }
 }
 
+// Shared-memory layout of a staged tile: row r (the items of thread r on the
+// item-parallel path, 128 bytes) holds 16-byte chunk j at position j ^ (r & 7),
+// so the eight rows a quarter-warp reads fall on different banks.
+template <typename T>
+__device__ __forceinline__ uint32_t segf_slot(uint32_t i) {
+    constexpr uint32_t EPC = 16 / sizeof(T);
+    const uint32_t c = i / EPC, r = c >> 3, j = c & 7;
+    return (((r << 3) | (j ^ (r & 7))) * EPC) + (i % EPC);
+}
+__device__ __forceinline__ uint32_t segf_chunk_slot(uint32_t c) { return ((c >> 3) << 3) | ((c & 7) ^ ((c >> 3) & 7)); }
+
 // Reduce items [lo, hi) of the staged tile (tile-relative) with one warp.
 template <typename Op, typename T>
 __device__ __forceinline__ T segf_warp_piece(const T* tile, uint32_t lo, uint32_t hi, int lane) {
     T acc = Op::template identity<T>();
-    for (uint32_t i = lo + lane; i < hi; i += 32) acc = Op::template apply<T>(acc, tile[i]);
+    for (uint32_t i = lo + lane; i < hi; i += 32) acc = Op::template apply<T>(acc, tile[segf_slot<T>(i)]);
     return warp_reduce<Op>(acc);
+}
+
+// (has a segment head, value) pairs of the item-parallel path: the value runs
+// from the last head seen (or from the start) to the end of the span.
+template <typename Op, typename T>
+__device__ __forceinline__ void segf_combine(bool& f, T& v, bool fn, T vn) {  // (f, v) = (f, v) then (fn, vn)
+    v = fn ? vn : Op::template apply<T>(v, vn);
+    f = f || fn;
 }
 
 template <typename Op, typename T>
@@ -222,29 +242,153 @@ segf_main_kernel(const T* __restrict__ in, T* __restrict__ out, const uint32_t* 
     constexpr uint32_t TI = SEGF_BYTES / sizeof(T);
     __shared__ __align__(16) T s_tile[TI];
     __shared__ uint32_t s_b[SEGF_CHUNK], s_e[SEGF_CHUNK];
+    constexpr uint32_t SEGF_HBW = TI / 32;  // head bitmap words
+    __shared__ uint32_t s_hb[SEGF_HBW];
+    __shared__ bool s_wf[SEGF_WARPS];
+    __shared__ T s_wv[SEGF_WARPS];
+    __shared__ uint32_t s_wk[SEGF_WARPS];
+    extern __shared__ uint16_t s_segat[];  // [TI] segment (relative to lo) starting at each head position
     if (t.hdr->flag) return;
     const uint64_t ntiles = t.hdr->ntiles;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const bool vec = (reinterpret_cast<uintptr_t>(in) & 15) == 0;
+    const uint64_t last_end = end[S - 1];  // the last tile ends at the last segment end
+    uint64_t nlo = 0, nhi = 0;              // segment range of the next tile, loaded one tile ahead
+    if (blockIdx.x < ntiles) {
+        nlo = blockIdx.x ? t.first[blockIdx.x] : 0;
+        nhi = t.first[blockIdx.x + 1];
+    }
     for (uint64_t c = blockIdx.x; c < ntiles; c += gridDim.x) {
         const uint64_t base = c * TI;
-        // tile items: the last tile ends at the last segment end
-        const uint64_t last_end = end[S - 1];
         const uint32_t cnt = (uint32_t)min((uint64_t)TI, last_end - base);
+        const uint64_t lo = nlo;
+        const uint64_t hi = nhi;  // exclusive; segment hi may cross the right edge
+        const uint64_t m = hi - lo;
+        const bool has_next = hi < S;      // segment hi starts in this tile or at its end
+        bool fast = m + 1 <= SEGF_CHUNK;   // uniform over the CTA
+        const uint32_t M = (uint32_t)m + (has_next ? 1u : 0u);
         __syncthreads();  // previous tile fully consumed
+        // the tile, and (item-parallel path) the offsets of its segments, in one cp.async group
         if (vec && cnt == TI) {
             constexpr int CH = SEGF_BYTES / 16;
             for (int k = threadIdx.x; k < CH; k += SEGF_THREADS)
-                cp_async16(reinterpret_cast<char*>(s_tile) + k * 16, reinterpret_cast<const char*>(in + base) + k * 16);
-            cp_async_commit();
+                cp_async16(reinterpret_cast<char*>(s_tile) + segf_chunk_slot(k) * 16,
+                           reinterpret_cast<const char*>(in + base) + k * 16);
         } else {
-            for (uint32_t k = threadIdx.x; k < cnt; k += SEGF_THREADS) s_tile[k] = in[base + k];
+            for (uint32_t k = threadIdx.x; k < cnt; k += SEGF_THREADS) s_tile[segf_slot<T>(k)] = in[base + k];
         }
-        const uint64_t lo = c ? t.first[c] : 0;
-        const uint64_t hi = t.first[c + 1];  // exclusive; segment hi may cross the right edge
+        if (fast) {
+            for (uint32_t k = threadIdx.x; k < M; k += SEGF_THREADS) {
+                cp_async4(s_b + k, begin + lo + k);
+                cp_async4(s_e + k, end + lo + k);
+            }
+            for (uint32_t k = threadIdx.x; k < SEGF_HBW; k += SEGF_THREADS) s_hb[k] = 0u;
+        }
+        cp_async_commit();
+        if (c + gridDim.x < ntiles) {
+            nlo = t.first[c + gridDim.x];
+            nhi = t.first[c + gridDim.x + 1];
+        }
         if (threadIdx.x == 0) { t.carry_seg[c] = SEGF_NONE; t.head_seg[c] = SEGF_NONE; }
         cp_async_wait_all();
         __syncthreads();
+        // ---- item-parallel path: contiguous segments, at most SEGF_CHUNK - 1 owned.
+        // Thread r reduces its IPL consecutive items, splitting them at segment
+        // heads (a bitmap of the owned segments' begins); the pieces are joined
+        // across threads by a segmented scan of (has head, value) pairs.
+        if (fast) {
+            bool ok = true;
+            for (uint32_t k = threadIdx.x; k < M; k += SEGF_THREADS) {
+                const uint64_t b = s_b[k], e = s_e[k];
+                if (k == 0 ? b > base : b != s_e[k - 1]) ok = false;
+                if (e > b && b >= base && b < base + cnt) {
+                    atomicOr(&s_hb[(uint32_t)(b - base) >> 5], 1u << ((b - base) & 31));
+                    s_segat[b - base] = (uint16_t)k;
+                }
+            }
+            fast = __syncthreads_and(ok);
+        }
+        if (fast) {
+            // piece of owned segment kk (index relative to lo) is complete: out, or the head piece
+            auto emit = [&](uint32_t kk, T v) {
+                if (s_b[kk] >= base) out[lo + kk] = Op::template apply<T>(init, v);
+                else { t.head[c] = v; t.head_seg[c] = (uint32_t)(lo + kk); }
+            };
+            for (uint32_t k = threadIdx.x; k < (uint32_t)m; k += SEGF_THREADS)
+                if (s_e[k] == s_b[k]) out[lo + k] = init;  // empty segments
+            constexpr uint32_t IPL = TI / SEGF_THREADS;  // 32 (4-byte) or 16 (8-byte) items per thread
+            constexpr uint32_t EPC = 16 / sizeof(T);
+            const uint32_t r = threadIdx.x, p0 = r * IPL;
+            T x[IPL];
+#pragma unroll
+            for (uint32_t j = 0; j < 8; ++j) {
+                const uint4 qv = reinterpret_cast<const uint4*>(s_tile)[(r << 3) | (j ^ (r & 7))];
+                const T* e = reinterpret_cast<const T*>(&qv);
+#pragma unroll
+                for (uint32_t u = 0; u < EPC; ++u) x[j * EPC + u] = e[u];
+            }
+            const uint32_t hb = IPL == 32 ? s_hb[r] : (s_hb[r >> 1] >> (16 * (r & 1))) & 0xFFFFu;
+            const uint32_t nv = cnt > p0 ? min(IPL, cnt - p0) : 0u;
+            T cur = Op::template identity<T>(), pre = cur;
+            bool hh = false;
+            uint32_t ks = 0;  // segment (relative to lo) of the current piece once a head was seen
+#pragma unroll
+            for (uint32_t j = 0; j < IPL; ++j) {
+                if (j < nv) {
+                    if ((hb >> j) & 1u) {
+                        if (hh) emit(ks, cur);
+                        else pre = cur;
+                        ks = s_segat[p0 + j];
+                        hh = true;
+                        cur = Op::template identity<T>();
+                    }
+                    cur = Op::template apply<T>(cur, x[j]);
+                }
+            }
+            // warp-inclusive segmented scan of (hh, cur, ks): value and segment of the open piece
+            bool fi = hh;
+            T vi = cur;
+            uint32_t ki = ks;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const bool fy = __shfl_up_sync(0xffffffffu, fi, o);
+                const T vy = __shfl_up_sync(0xffffffffu, vi, o);
+                const uint32_t ky = __shfl_up_sync(0xffffffffu, ki, o);
+                if (lane >= o) {
+                    if (!fi) { vi = Op::template apply<T>(vy, vi); ki = ky; }
+                    fi = fi || fy;
+                }
+            }
+            bool fx = __shfl_up_sync(0xffffffffu, fi, 1);
+            T vx = __shfl_up_sync(0xffffffffu, vi, 1);
+            uint32_t kx = __shfl_up_sync(0xffffffffu, ki, 1);
+            if (lane == 0) { fx = false; vx = Op::template identity<T>(); kx = 0; }
+            if (lane == 31) { s_wf[warp] = fi; s_wv[warp] = vi; s_wk[warp] = ki; }
+            __syncthreads();
+            bool fc = false;  // no head before: the open piece belongs to segment lo
+            T vc = Op::template identity<T>();
+            uint32_t kc = 0;
+            for (int w = 0; w < warp; ++w) {
+                if (s_wf[w]) { vc = s_wv[w]; kc = s_wk[w]; fc = true; }
+                else vc = Op::template apply<T>(vc, s_wv[w]);
+            }
+            if (fx) { vc = vx; kc = kx; fc = true; }
+            else vc = Op::template apply<T>(vc, vx);
+            // vc, kc: the piece open where this thread's items begin
+            // the first head closes the piece before it (empty when the head is at tile position 0)
+            if (hh && !(p0 == 0 && (hb & 1u))) emit(kc, Op::template apply<T>(vc, pre));
+            if (threadIdx.x == SEGF_THREADS - 1) {  // the piece open at the tile end
+                if (hh) { vc = cur; kc = ks; }
+                else vc = Op::template apply<T>(vc, cur);
+                if (has_next && c + 1 < ntiles && kc == M - 1) {  // segment hi crosses the right edge
+                    t.carry[c] = vc;
+                    t.carry_seg[c] = (uint32_t)hi;
+                } else {
+                    emit(kc, vc);
+                }
+            }
+            continue;
+        }
         // segments owned by this tile (end inside it), in chunks of offsets
         for (uint64_t s0 = lo; s0 < hi; s0 += SEGF_CHUNK) {
             const uint32_t m = (uint32_t)min((uint64_t)SEGF_CHUNK, hi - s0);
@@ -279,16 +423,18 @@ __global__ void __launch_bounds__(256)
 segf_fixup_kernel(T* __restrict__ out, const uint32_t* __restrict__ begin, T init, SegfTemp<T> t) {
     constexpr uint64_t TI = SEGF_BYTES / sizeof(T);
     if (t.hdr->flag) return;
-    const uint64_t c = (uint64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (c >= t.hdr->ntiles) return;
-    const uint32_t s = t.head_seg[c];
-    if (s == SEGF_NONE) return;
-    const uint64_t c0 = begin[s] / TI;
-    T acc = Op::template identity<T>();
-    for (uint64_t k = c0 + lane; k < c; k += 32) acc = Op::template apply<T>(acc, t.carry[k]);
-    acc = warp_reduce<Op>(acc);
-    if (lane == 0) out[s] = Op::template apply<T>(Op::template apply<T>(init, acc), t.head[c]);
+    const uint64_t ntiles = t.hdr->ntiles;
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+    for (uint64_t c = (uint64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); c < ntiles; c += warps) {
+        const uint32_t s = t.head_seg[c];
+        if (s == SEGF_NONE) continue;
+        const uint64_t c0 = begin[s] / TI;
+        T acc = Op::template identity<T>();
+        for (uint64_t k = c0 + lane; k < c; k += 32) acc = Op::template apply<T>(acc, t.carry[k]);
+        acc = warp_reduce<Op>(acc);
+        if (lane == 0) out[s] = Op::template apply<T>(Op::template apply<T>(init, acc), t.head[c]);
+    }
 }
 
 template <typename Op, typename T>
@@ -317,11 +463,15 @@ static lcpp_status segf_launch(const void* in, void* out, uint64_t S, const uint
     if (cudaMemsetAsync(t.hdr, 0, sizeof(SegfHdr), s) != cudaSuccess) return LCPP_ERR_CUDA;
     { ProfScope ps("seg_partition", s);
     segf_partition_kernel<T><<<(unsigned)ceil_div(S, 256), 256, 0, s>>>(begin, end, S, t); }
+    constexpr int SEGAT = (SEGF_BYTES / sizeof(T)) * sizeof(uint16_t);
+    if (cudaFuncSetAttribute(segf_main_kernel<Op, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SEGAT) != cudaSuccess)
+        return LCPP_ERR_CUDA;
     { ProfScope ps("seg_flat", s);
-    segf_main_kernel<Op, T><<<(unsigned)(di.sms * SEGF_CTAS_PER_SM), SEGF_THREADS, 0, s>>>(
+    segf_main_kernel<Op, T><<<(unsigned)(di.sms * SEGF_CTAS_PER_SM), SEGF_THREADS, SEGAT, s>>>(
         (const T*)in, (T*)out, begin, end, S, init, t); }
     { ProfScope ps("seg_fixup", s);
-    segf_fixup_kernel<Op, T><<<(unsigned)ceil_div(t.cap, 8), 256, 0, s>>>((T*)out, begin, init, t);
+    const uint64_t fix_grid = std::min<uint64_t>(ceil_div(t.cap, 8), (uint64_t)di.sms * 8);  // warps stride over the tiles
+    segf_fixup_kernel<Op, T><<<(unsigned)(fix_grid ? fix_grid : 1), 256, 0, s>>>((T*)out, begin, init, t);
     segf_fallback_kernel<Op, T><<<(unsigned)(di.sms * 4), 256, 0, s>>>((const T*)in, (T*)out, S, begin, end, init,
                                                                        t.hdr); }
     count_launch(4);
