@@ -172,3 +172,30 @@ def test_flat_path_edges(cuda):
     # 8-byte values (4096-item tiles)
     x8 = G.u64(int(off[-1]), seed=24).view(np.int64)
     assert np.array_equal(_abi_seg_custom(0, x8, b, e), oracle.segment_reduce(0, x8, b, e))
+
+
+@pytest.mark.gpu
+def test_item_parallel_tiles(cuda):
+    """Contiguous offsets: tiles of short segments (item-parallel path), heads on
+    32-item thread boundaries and at tile starts, empty runs, and tiles with more
+    than 511 segments (per-segment path) in one input."""
+    rng = np.random.default_rng(31)
+    TI = 8192
+    a = rng.integers(0, 41, size=3000)                       # ~400 segments per tile
+    a = np.concatenate([a, [TI - int(a.sum()) % TI]])         # the next segment starts a tile
+    parts = [a,
+             np.full(600, 32),                                # heads on thread boundaries
+             np.array([TI - (600 * 32) % TI, 0, 0, TI]),      # heads at tile starts, empty runs
+             rng.integers(0, 2, size=3000),                   # > 511 segments per tile
+             rng.integers(1, 3000, size=300)]                 # long pieces crossing tiles
+    lens = np.concatenate(parts).astype(np.uint64)
+    off = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+    b, e = off[:-1], off[1:]
+    xi = G.u32(int(off[-1]), seed=32).view(np.int32)
+    for op in (0, 1, 2):
+        assert np.array_equal(_abi_seg_custom(op, xi, b, e), oracle.segment_reduce(op, xi, b, e))
+    xf = G.f32_unit(int(off[-1]), seed=33)
+    np.testing.assert_allclose(_abi_seg_custom(0, xf, b, e).astype(np.float64), oracle.segment_reduce(0, xf, b, e),
+                               rtol=1e-5, atol=0)
+    x8 = G.u64(int(off[-1]), seed=34).view(np.int64)
+    assert np.array_equal(_abi_seg_custom(2, x8, b, e), oracle.segment_reduce(2, x8, b, e))
