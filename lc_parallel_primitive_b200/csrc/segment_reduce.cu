@@ -332,18 +332,25 @@ segf_main_kernel(const T* __restrict__ in, T* __restrict__ out, const uint32_t* 
             T cur = Op::template identity<T>(), pre = cur;
             bool hh = false;
             uint32_t ks = 0;  // segment (relative to lo) of the current piece once a head was seen
-#pragma unroll
-            for (uint32_t j = 0; j < IPL; ++j) {
-                if (j < nv) {
-                    if ((hb >> j) & 1u) {
-                        if (hh) emit(ks, cur);
-                        else pre = cur;
-                        ks = s_segat[p0 + j];
-                        hh = true;
-                        cur = Op::template identity<T>();
-                    }
-                    cur = Op::template apply<T>(cur, x[j]);
+            // a head closes the piece before it; a piece begun at a head inside
+            // this thread's items started in the tile, so it goes straight to out
+            auto step = [&](uint32_t j) {
+                const bool hd = (hb >> j) & 1u;
+                if (hd) {
+                    if (hh) out[lo + ks] = Op::template apply<T>(init, cur);
+                    else pre = cur;
+                    ks = s_segat[p0 + j];
+                    hh = true;
                 }
+                cur = hd ? x[j] : Op::template apply<T>(cur, x[j]);
+            };
+            if (nv == IPL) {
+#pragma unroll
+                for (uint32_t j = 0; j < IPL; ++j) step(j);
+            } else {
+#pragma unroll
+                for (uint32_t j = 0; j < IPL; ++j)
+                    if (j < nv) step(j);
             }
             // warp-inclusive segmented scan of (hh, cur, ks): value and segment of the open piece
             bool fi = hh;
