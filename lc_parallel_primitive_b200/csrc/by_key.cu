@@ -29,10 +29,10 @@
 //    warp-wide look-back (32 predecessors per poll, ordered reduction because
 //    the pair operator does not commute).
 //  * Descriptors: for 4-byte values and n < 2^30 one 64-bit word per tile
-//    {status | count | value} with relaxed accesses (no fences); otherwise a
-//    status word per tile plus separate partial and inclusive pair slots, a
-//    slot written before its status with release semantics and read after an
-//    acquire load of the status.  Every wait is bounded by g_spin_limit.
+//    {status | count | value} with relaxed accesses (no fences); otherwise
+//    two or three relaxed words per tile, each carrying the status beside one
+//    part of the pair, accepted when all statuses match.  Every wait is
+//    bounded by g_spin_limit.
 //  * Outputs are staged in shared memory and written coalesced: the scanned
 //    values back through the same swizzle, the runs of ReduceByKey compacted
 //    to a dense range per tile.

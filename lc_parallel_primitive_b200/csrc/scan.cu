@@ -318,8 +318,8 @@ static lcpp_status scan_impl(int kind, int op, int dtype, const void* in, void* 
         using Op = decltype(opv);
         using D = ScanDesc<T>;
         const uint64_t tiles = aligned ? desc_tiles : ceil_div(n, scan_tile_items<T>());
-        // zero the ticket and the descriptors (for 8-byte values the status words)
-        const size_t zero_bytes = SCAN_HDR + (sizeof(T) == 4 ? tiles * 8 : tiles * 4);
+        // zero the ticket and the descriptors (one 64-bit word per tile, two for 8-byte values)
+        const size_t zero_bytes = SCAN_HDR + tiles * (sizeof(T) == 4 ? 8 : 16);
         if (cudaMemsetAsync(temp, 0, zero_bytes, s) != cudaSuccess) return LCPP_ERR_CUDA;
         const D desc = D::carve(desc_mem, desc_tiles);
         const T iv = init ? *(const T*)init : Op::template identity<T>();

@@ -5,7 +5,8 @@ import pytest
 
 import oracle
 from lc_parallel_primitive_b200 import datagen as G
-from tests.helpers import abi_scan, assert_float_sum_close, to_host
+from lc_parallel_primitive_b200 import _lib as L
+from tests.helpers import NP2LCPP, abi_scan, assert_float_sum_close, stream, to_dev, to_host
 
 pytestmark = pytest.mark.gpu
 
@@ -71,6 +72,35 @@ def test_double_scan_tolerance(cuda, inclusive):
         x = G.f32_normal(n, seed=250 + i).astype(np.float64) * np.float64(1.0 + 1e-9)
         got = abi_scan(inclusive, x, offset_elems=i % 2)
         assert_float_sum_close(got, oracle.scan(inclusive, x), oracle.abs_prefix(x), rel=1e-12)
+
+
+@pytest.mark.parametrize("dtype", [np.uint32, np.uint64, np.float64])
+def test_temp_reused_across_calls(cuda, dtype):
+    """A temp buffer left with another call's published descriptors (and one
+    filled with 0xff bytes) must give the same results: each call clears every
+    descriptor it reads."""
+    import torch
+
+    lib = L.lib()
+    n = 5 * 8192 + 77
+    dt = NP2LCPP[np.dtype(dtype)]
+    tb = lib.lcpp_scan_temp_bytes(dt, n)
+    t = torch.full((tb,), 0xFF, dtype=torch.uint8, device="cuda")
+    for seed in (401, 402, 403):
+        x = G.u64(n, seed=seed).view(np.uint64)
+        x = (x % 1000).astype(dtype) if dtype != np.uint32 else G.u32(n, seed=seed)
+        for off in (0, 1):
+            d = to_dev(x, off)
+            out = torch.empty_like(d)
+            L.check(lib.lcpp_scan(0, dt, d.data_ptr(), out.data_ptr(), n, t.data_ptr(), tb, stream()))
+            torch.cuda.synchronize()
+            L.check(lib.lcpp_last_device_error(stream()))
+            got = out.cpu().numpy().view(np.dtype(dtype))
+            want = oracle.scan(False, x)
+            if dtype == np.float64:
+                np.testing.assert_allclose(got, want, rtol=1e-12, atol=1e-9)
+            else:
+                assert np.array_equal(got, want), (seed, off)
 
 
 def test_8byte_scan_full_size(cuda):
