@@ -132,17 +132,21 @@ seg_block_kernel(const T* __restrict__ in, T* __restrict__ out,
 //    SEGF_BYTES tile (the first whose end is past the tile start), the tile
 //    count, and a flag if the offsets are not monotone or the tiles do not fit
 //    the temp buffer;
-//  * segf_main_kernel (persistent): a tile's items land in shared memory by
-//    cp.async, then one warp per segment piece reduces it (lane-strided, then
-//    a shuffle tree).  A segment wholly inside the tile is written at once; a
+//  * segf_main_kernel (persistent): a tile's items (and its segments'
+//    offsets) land in shared memory by cp.async.  When the tile's segments
+//    are contiguous, each thread reduces 32 consecutive items split at
+//    segment heads and the pieces are joined by a segmented scan; otherwise
+//    one warp per segment piece reduces it (lane-strided, then a shuffle
+//    tree).  A segment wholly inside the tile is written at once; a
 //    segment that crosses the tile's right edge leaves its piece in carry[c];
 //    one that enters from the left leaves it in head[c];
 //  * segf_fixup_kernel (one warp per tile with a head piece): out[s] = init
 //    (+) carries of the tiles the segment crosses (lane-strided, shuffle tree)
 //    (+) head piece.  Every combination order is fixed, so float results do
 //    not depend on scheduling;
-//  * segf_fallback_kernel: when the flag is set, one warp per segment as
-//    above; otherwise it returns at once.
+//    When the flag is set the same kernel reduces one warp per segment
+//    instead (the fallback).  The three kernels are chained by programmatic
+//    dependent launch, so each one's launch overlaps the previous kernel.
 // ---------------------------------------------------------------------------
 constexpr int SEGF_THREADS = 256;
 constexpr int SEGF_WARPS = SEGF_THREADS / 32;
@@ -191,6 +195,8 @@ __global__ void __launch_bounds__(256)
 segf_partition_kernel(const uint32_t* __restrict__ begin, const uint32_t* __restrict__ end, uint64_t S,
                       SegfTemp<T> t) {
     constexpr uint64_t TI = SEGF_BYTES / sizeof(T);
+    // the tile kernel may be scheduled now; its griddepcontrol.wait still waits for this grid's writes
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint64_t s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= S) return;
     const uint64_t e = end[s], b = begin[s];
@@ -248,6 +254,8 @@ segf_main_kernel(const T* __restrict__ in, T* __restrict__ out, const uint32_t* 
     __shared__ T s_wv[SEGF_WARPS];
     __shared__ uint32_t s_wk[SEGF_WARPS];
     extern __shared__ uint16_t s_segat[];  // [TI] segment (relative to lo) starting at each head position
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the partition kernel has completed
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (t.hdr->flag) return;
     const uint64_t ntiles = t.hdr->ntiles;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -425,15 +433,29 @@ segf_main_kernel(const T* __restrict__ in, T* __restrict__ out, const uint32_t* 
     }
 }
 
+// Fix-up, or (flag set by the partition kernel) the per-segment fallback.
 template <typename Op, typename T>
 __global__ void __launch_bounds__(256)
-segf_fixup_kernel(T* __restrict__ out, const uint32_t* __restrict__ begin, T init, SegfTemp<T> t) {
+segf_fixup_kernel(const T* __restrict__ in, T* __restrict__ out, uint64_t S, const uint32_t* __restrict__ begin,
+                  const uint32_t* __restrict__ end, T init, SegfTemp<T> t) {
     constexpr uint64_t TI = SEGF_BYTES / sizeof(T);
-    if (t.hdr->flag) return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the tile kernel has completed
     const int lane = threadIdx.x & 31;
-    const uint64_t ntiles = t.hdr->ntiles;
     const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
-    for (uint64_t c = (uint64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); c < ntiles; c += warps) {
+    const uint64_t gw = (uint64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (t.hdr->flag) {  // offsets not monotone or tiles beyond the temp: one warp per segment
+        for (uint64_t sg = gw; sg < S; sg += warps) {
+            uint64_t b = begin[sg], e = end[sg];
+            if (e < b) e = b;
+            T acc = Op::template identity<T>();
+            for (uint64_t i = b + lane; i < e; i += 32) acc = Op::template apply<T>(acc, ldcs(in + i));
+            acc = warp_reduce<Op>(acc);
+            if (lane == 0) out[sg] = Op::template apply<T>(init, acc);
+        }
+        return;
+    }
+    const uint64_t ntiles = t.hdr->ntiles;
+    for (uint64_t c = gw; c < ntiles; c += warps) {
         const uint32_t s = t.head_seg[c];
         if (s == SEGF_NONE) continue;
         const uint64_t c0 = begin[s] / TI;
@@ -444,21 +466,22 @@ segf_fixup_kernel(T* __restrict__ out, const uint32_t* __restrict__ begin, T ini
     }
 }
 
-template <typename Op, typename T>
-__global__ void __launch_bounds__(256)
-segf_fallback_kernel(const T* __restrict__ in, T* __restrict__ out, uint64_t S, const uint32_t* __restrict__ begin,
-                     const uint32_t* __restrict__ end, T init, const SegfHdr* hdr) {
-    if (!hdr->flag) return;
-    const int lane = threadIdx.x & 31;
-    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
-    for (uint64_t s = (uint64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); s < S; s += warps) {
-        uint64_t b = begin[s], e = end[s];
-        if (e < b) e = b;
-        T acc = Op::template identity<T>();
-        for (uint64_t i = b + lane; i < e; i += 32) acc = Op::template apply<T>(acc, ldcs(in + i));
-        acc = warp_reduce<Op>(acc);
-        if (lane == 0) out[s] = Op::template apply<T>(init, acc);
-    }
+// Launch with programmatic dependent launch: the kernel may start while the
+// previous kernel on the stream runs and waits for it with griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+static cudaError_t segf_launch_pdl(void (*k)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t s,
+                                   Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
 template <typename Op, typename T>
@@ -474,14 +497,14 @@ static lcpp_status segf_launch(const void* in, void* out, uint64_t S, const uint
     if (cudaFuncSetAttribute(segf_main_kernel<Op, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SEGAT) != cudaSuccess)
         return LCPP_ERR_CUDA;
     { ProfScope ps("seg_flat", s);
-    segf_main_kernel<Op, T><<<(unsigned)(di.sms * SEGF_CTAS_PER_SM), SEGF_THREADS, SEGAT, s>>>(
-        (const T*)in, (T*)out, begin, end, S, init, t); }
+    if (segf_launch_pdl(segf_main_kernel<Op, T>, (unsigned)(di.sms * SEGF_CTAS_PER_SM), SEGF_THREADS, SEGAT, s,
+                        (const T*)in, (T*)out, begin, end, S, init, t) != cudaSuccess)
+        return LCPP_ERR_CUDA; }
     { ProfScope ps("seg_fixup", s);
-    const uint64_t fix_grid = std::min<uint64_t>(ceil_div(t.cap, 8), (uint64_t)di.sms * 8);  // warps stride over the tiles
-    segf_fixup_kernel<Op, T><<<(unsigned)(fix_grid ? fix_grid : 1), 256, 0, s>>>((T*)out, begin, init, t);
-    segf_fallback_kernel<Op, T><<<(unsigned)(di.sms * 4), 256, 0, s>>>((const T*)in, (T*)out, S, begin, end, init,
-                                                                       t.hdr); }
-    count_launch(4);
+    if (segf_launch_pdl(segf_fixup_kernel<Op, T>, (unsigned)(di.sms * 8), 256, 0, s, (const T*)in, (T*)out, S, begin,
+                        end, init, t) != cudaSuccess)
+        return LCPP_ERR_CUDA; }
+    count_launch(3);
     return check_launch();
 }
 
