@@ -44,9 +44,17 @@ constexpr int RS_WARPS = RS_THREADS / 32;
 constexpr int RS_MAX_PASSES = 8;
 constexpr int RS_LB_WINDOW = 8;  // predecessor words loaded per look-back step
 
-template <typename KB> struct RsItems;
-template <> struct RsItems<uint32_t> { static constexpr int value = 16; };
-template <> struct RsItems<uint64_t> { static constexpr int value = 8; };
+// Keys per thread of a onesweep tile.  Keys-only sorts stage no values, so
+// their tiles hold twice the keys in the same shared memory (fewer tiles,
+// shorter look-back chains).
+#ifndef LCPP_RS_KO_ITEMS
+#define LCPP_RS_KO_ITEMS 32
+#endif
+template <typename KB, bool KEYS_ONLY = false> struct RsItems;
+template <> struct RsItems<uint32_t, false> { static constexpr int value = 16; };
+template <> struct RsItems<uint64_t, false> { static constexpr int value = 8; };
+template <> struct RsItems<uint32_t, true> { static constexpr int value = LCPP_RS_KO_ITEMS; };
+template <> struct RsItems<uint64_t, true> { static constexpr int value = LCPP_RS_KO_ITEMS / 2; };
 
 struct NoValue {};
 
@@ -227,7 +235,7 @@ struct RsPass {
 
 template <typename KB, typename VB, int THREADS, bool DIG = false>
 constexpr size_t rs_smem_bytes() {
-    constexpr int TILE = THREADS * RsItems<KB>::value;
+    constexpr int TILE = THREADS * RsItems<KB, std::is_same<VB, NoValue>::value>::value;
     return (DIG ? (size_t)TILE : 0) + (size_t)TILE * sizeof(KB) +
            (std::is_same<VB, NoValue>::value ? 0 : (size_t)TILE * sizeof(VB)) +
            (size_t)(THREADS / 32) * RS_DIGITS * 4 * 2 + RS_DIGITS * 4 * 2 + 64;
@@ -255,7 +263,7 @@ __device__ __forceinline__ void rs_copy_tile(const void* src, void* dst, uint64_
 template <typename KB, typename VB, typename W, int KIND, bool DESC, int THREADS, bool DIG = false>
 __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(RsPass a) {
     constexpr int RS_WARPS = THREADS / 32;
-    constexpr int ITEMS = RsItems<KB>::value;
+    constexpr int ITEMS = RsItems<KB, std::is_same<VB, NoValue>::value>::value;
     constexpr int TILE = THREADS * ITEMS;
     constexpr bool HAS_V = !std::is_same<VB, NoValue>::value;
     using F = LbFlags<W>;
@@ -500,7 +508,8 @@ struct RsLayout {
 
 static RsLayout rs_layout(size_t ksize, size_t vsize, uint64_t n, uint32_t passes) {
     RsLayout L{};
-    const int items = ksize == 4 ? RsItems<uint32_t>::value : RsItems<uint64_t>::value;
+    const int items = ksize == 4 ? (vsize ? RsItems<uint32_t>::value : RsItems<uint32_t, true>::value)
+                                 : (vsize ? RsItems<uint64_t>::value : RsItems<uint64_t, true>::value);
     L.passes = passes;
     L.tiles = ceil_div(n ? n : 1, (uint64_t)RS_THREADS * items);
     L.lb_word = n < (1ull << 30) ? 4 : 8;
