@@ -44,19 +44,19 @@ constexpr int RS_WARPS = RS_THREADS / 32;
 constexpr int RS_MAX_PASSES = 8;
 constexpr int RS_LB_WINDOW = 8;  // predecessor words loaded per look-back step
 
-// Keys per thread of a onesweep tile.  Keys-only sorts stage no values, so
-// their tiles hold twice the keys in the same shared memory (fewer tiles,
-// shorter look-back chains).
-#ifndef LCPP_RS_KO_ITEMS
-#define LCPP_RS_KO_ITEMS 32
-#endif
-template <typename KB, bool KEYS_ONLY = false> struct RsItems;
-template <> struct RsItems<uint32_t, false> { static constexpr int value = 16; };
-template <> struct RsItems<uint64_t, false> { static constexpr int value = 8; };
-template <> struct RsItems<uint32_t, true> { static constexpr int value = LCPP_RS_KO_ITEMS; };
-template <> struct RsItems<uint64_t, true> { static constexpr int value = LCPP_RS_KO_ITEMS / 2; };
-
 struct NoValue {};
+
+// Keys per thread of a onesweep tile, by the bytes an item moves (key +
+// value): a tile stages 64-72 KiB of keys and values, so two CTAs fit an SM
+// beside the rank words, and fewer, larger tiles shorten the look-back
+// chains (keys-only u32: 32; u32 pairs or u64 keys only: 16; one 8-byte and
+// one 4-byte half: 12; 16-byte pairs: 8).
+constexpr int rs_items_for(size_t key_bytes, size_t value_bytes) {
+    return key_bytes + value_bytes <= 4 ? 32 : key_bytes + value_bytes <= 8 ? 16 : key_bytes + value_bytes <= 12 ? 12 : 8;
+}
+template <typename KB, typename VB> struct RsItems {
+    static constexpr int value = rs_items_for(sizeof(KB), std::is_same<VB, NoValue>::value ? 0 : sizeof(VB));
+};
 
 // Map key bits to an unsigned order-preserving image (ascending), or its
 // complement for descending.  KIND: 0 unsigned, 1 signed, 2 floating point.
@@ -235,7 +235,7 @@ struct RsPass {
 
 template <typename KB, typename VB, int THREADS, bool DIG = false>
 constexpr size_t rs_smem_bytes() {
-    constexpr int TILE = THREADS * RsItems<KB, std::is_same<VB, NoValue>::value>::value;
+    constexpr int TILE = THREADS * RsItems<KB, VB>::value;
     return (DIG ? (size_t)TILE : 0) + (size_t)TILE * sizeof(KB) +
            (std::is_same<VB, NoValue>::value ? 0 : (size_t)TILE * sizeof(VB)) +
            (size_t)(THREADS / 32) * RS_DIGITS * 4 * 2 + RS_DIGITS * 4 * 2 + 64;
@@ -263,7 +263,7 @@ __device__ __forceinline__ void rs_copy_tile(const void* src, void* dst, uint64_
 template <typename KB, typename VB, typename W, int KIND, bool DESC, int THREADS, bool DIG = false>
 __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(RsPass a) {
     constexpr int RS_WARPS = THREADS / 32;
-    constexpr int ITEMS = RsItems<KB, std::is_same<VB, NoValue>::value>::value;
+    constexpr int ITEMS = RsItems<KB, VB>::value;
     constexpr int TILE = THREADS * ITEMS;
     constexpr bool HAS_V = !std::is_same<VB, NoValue>::value;
     using F = LbFlags<W>;
@@ -508,8 +508,7 @@ struct RsLayout {
 
 static RsLayout rs_layout(size_t ksize, size_t vsize, uint64_t n, uint32_t passes) {
     RsLayout L{};
-    const int items = ksize == 4 ? (vsize ? RsItems<uint32_t>::value : RsItems<uint32_t, true>::value)
-                                 : (vsize ? RsItems<uint64_t>::value : RsItems<uint64_t, true>::value);
+    const int items = rs_items_for(ksize, vsize);
     L.passes = passes;
     L.tiles = ceil_div(n ? n : 1, (uint64_t)RS_THREADS * items);
     L.lb_word = n < (1ull << 30) ? 4 : 8;
