@@ -49,10 +49,13 @@ struct NoValue {};
 // Keys per thread of a onesweep tile, by the bytes an item moves (key +
 // value): a tile stages 64-72 KiB of keys and values, so two CTAs fit an SM
 // beside the rank words, and fewer, larger tiles shorten the look-back
-// chains (keys-only u32: 32; u32 pairs or u64 keys only: 16; one 8-byte and
-// one 4-byte half: 12; 16-byte pairs: 8).
+// chains (keys-only u32: 32; u32 pairs or u64 keys only: 18; one 8-byte and
+// one 4-byte half: 12; 16-byte pairs: 8).  LCPP_RS_I8 overrides the 8-byte case.
+#ifndef LCPP_RS_I8
+#define LCPP_RS_I8 18
+#endif
 constexpr int rs_items_for(size_t key_bytes, size_t value_bytes) {
-    return key_bytes + value_bytes <= 4 ? 32 : key_bytes + value_bytes <= 8 ? 16 : key_bytes + value_bytes <= 12 ? 12 : 8;
+    return key_bytes + value_bytes <= 4 ? 32 : key_bytes + value_bytes <= 8 ? LCPP_RS_I8 : key_bytes + value_bytes <= 12 ? 12 : 8;
 }
 template <typename KB, typename VB> struct RsItems {
     static constexpr int value = rs_items_for(sizeof(KB), std::is_same<VB, NoValue>::value ? 0 : sizeof(VB));
