@@ -54,11 +54,16 @@ struct NoValue {};
 #ifndef LCPP_RS_I8
 #define LCPP_RS_I8 18
 #endif
-constexpr int rs_items_for(size_t key_bytes, size_t value_bytes) {
-    return key_bytes + value_bytes <= 4 ? 32 : key_bytes + value_bytes <= 8 ? LCPP_RS_I8 : key_bytes + value_bytes <= 12 ? 12 : 8;
+// Passes over precomputed digits (DIG) also stage one digit byte per item, so
+// their tiles are smaller where the 8-byte and 4-byte sizes would not fit two
+// CTAs per SM.
+constexpr int rs_items_for(size_t key_bytes, size_t value_bytes, bool dig = false) {
+    return key_bytes + value_bytes <= 4 ? (dig ? 28 : 32)
+         : key_bytes + value_bytes <= 8 ? (dig ? 16 : LCPP_RS_I8)
+         : key_bytes + value_bytes <= 12 ? 12 : 8;
 }
-template <typename KB, typename VB> struct RsItems {
-    static constexpr int value = rs_items_for(sizeof(KB), std::is_same<VB, NoValue>::value ? 0 : sizeof(VB));
+template <typename KB, typename VB, bool DIG = false> struct RsItems {
+    static constexpr int value = rs_items_for(sizeof(KB), std::is_same<VB, NoValue>::value ? 0 : sizeof(VB), DIG);
 };
 
 // Map key bits to an unsigned order-preserving image (ascending), or its
@@ -238,7 +243,7 @@ struct RsPass {
 
 template <typename KB, typename VB, int THREADS, bool DIG = false>
 constexpr size_t rs_smem_bytes() {
-    constexpr int TILE = THREADS * RsItems<KB, VB>::value;
+    constexpr int TILE = THREADS * RsItems<KB, VB, DIG>::value;
     return (DIG ? (size_t)TILE : 0) + (size_t)TILE * sizeof(KB) +
            (std::is_same<VB, NoValue>::value ? 0 : (size_t)TILE * sizeof(VB)) +
            (size_t)(THREADS / 32) * RS_DIGITS * 4 * 2 + RS_DIGITS * 4 * 2 + 64;
@@ -266,7 +271,7 @@ __device__ __forceinline__ void rs_copy_tile(const void* src, void* dst, uint64_
 template <typename KB, typename VB, typename W, int KIND, bool DESC, int THREADS, bool DIG = false>
 __global__ void __launch_bounds__(THREADS, 1024 / THREADS) rs_onesweep_kernel(RsPass a) {
     constexpr int RS_WARPS = THREADS / 32;
-    constexpr int ITEMS = RsItems<KB, VB>::value;
+    constexpr int ITEMS = RsItems<KB, VB, DIG>::value;
     constexpr int TILE = THREADS * ITEMS;
     constexpr bool HAS_V = !std::is_same<VB, NoValue>::value;
     using F = LbFlags<W>;
@@ -509,9 +514,9 @@ struct RsLayout {
     size_t bins_off, ticket_off, lb_off, keys_off, vals_off, total, zero_bytes;
 };
 
-static RsLayout rs_layout(size_t ksize, size_t vsize, uint64_t n, uint32_t passes) {
+static RsLayout rs_layout(size_t ksize, size_t vsize, uint64_t n, uint32_t passes, bool dig = false) {
     RsLayout L{};
-    const int items = rs_items_for(ksize, vsize);
+    const int items = rs_items_for(ksize, vsize, dig);
     L.passes = passes;
     L.tiles = ceil_div(n ? n : 1, (uint64_t)RS_THREADS * items);
     L.lb_word = n < (1ull << 30) ? 4 : 8;
@@ -682,7 +687,7 @@ static lcpp_status rs_sort_impl(int key_dtype, int value_dtype, int descending,
     if (!keys_in || !keys_out || (vs && (!values_in || !values_out))) return LCPP_ERR_INVALID_ARG;
     // Temp is sized for a full-width sort; fewer bits need no more.
     if (!temp || temp_bytes < lcpp_radix_sort_temp_bytes(key_dtype, value_dtype, n)) return LCPP_ERR_TEMP_TOO_SMALL;
-    const RsLayout L = rs_layout(ks, vs, n, passes);
+    const RsLayout L = rs_layout(ks, vs, n, passes, digits != nullptr);
     cudaStream_t s = (cudaStream_t)stream;
     char* t = (char*)temp;
     const bool desc = descending != 0;
