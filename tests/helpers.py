@@ -144,7 +144,7 @@ def abi_segment_reduce_fixed(op, x_np, num_segments, seg_size):
     return to_host(out)
 
 
-def abi_scan_by_key(inclusive, op, keys_np, values_np, init=None, offset_elems=0, in_place=False):
+def abi_scan_by_key(inclusive, op, keys_np, values_np, init=None, offset_elems=0, in_place=False, temp_buf=None):
     import torch
 
     lib = L.lib()
@@ -154,7 +154,7 @@ def abi_scan_by_key(inclusive, op, keys_np, values_np, init=None, offset_elems=0
     v = to_dev(values_np, offset_elems)
     out = v if in_place else empty_dev(n, values_np.dtype, offset_elems)
     tb = lib.lcpp_scan_by_key_temp_bytes(kdt, vdt, n)
-    t = temp(tb)
+    t = temp(tb) if temp_buf is None else temp_buf  # a caller's buffer may hold another call's state
     iv = None if init is None else np.array([init], dtype=values_np.dtype)
     L.check(lib.lcpp_scan_by_key(L.SCAN_INCLUSIVE if inclusive else L.SCAN_EXCLUSIVE, op, kdt, vdt,
                                  k.data_ptr(), v.data_ptr(), out.data_ptr(), n,

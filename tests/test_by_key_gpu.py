@@ -115,6 +115,27 @@ def test_scan_by_key_dtypes(cuda, kdt, vdt):
                 check_scan(got, keys, vals, inclusive, op, None)
 
 
+@pytest.mark.parametrize("vdt", [np.int32, np.int64, np.float64])
+def test_scan_by_key_temp_reused(cuda, vdt):
+    """One temp buffer, first filled with 0xff bytes, then left with each
+    call's published descriptors, serves the next calls: every call clears the
+    descriptors it reads."""
+    import torch
+
+    from lc_parallel_primitive_b200 import _lib as L
+    from tests.helpers import NP2LCPP
+
+    n = 7 * 4096 + 333
+    tb = L.lib().lcpp_scan_by_key_temp_bytes(NP2LCPP[np.dtype(np.int32)], NP2LCPP[np.dtype(vdt)], n)
+    t = torch.full((tb,), 0xFF, dtype=torch.uint8, device="cuda")
+    for j in range(3):
+        keys = run_keys(n, 7 + j, np.int32, seed=300 + j)
+        vals = values_of(n, vdt, seed=310 + j)
+        for off in (0, 1):
+            got = abi_scan_by_key(False, 0, keys, vals, offset_elems=off, temp_buf=t)
+            check_scan(got, keys, vals, False, 0, None)
+
+
 @pytest.mark.parametrize("kdt", KEY_DTYPES)
 @pytest.mark.parametrize("vdt", VALUE_DTYPES)
 def test_reduce_by_key_dtypes(cuda, kdt, vdt):
