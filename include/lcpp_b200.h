@@ -276,8 +276,9 @@ lcpp_status lcpp_mg_scan(int kind, int dtype, const void* in, void* out, uint64_
  * (key, rank, index), so slices are near n_total / nranks whatever the key
  * distribution, duplicates included; a slice longer than capacity returns
  * LCPP_ERR_CAPACITY.  At most 256 ranks.  Slices move by CUDA IPC pulls (copy
- * engines) when every rank's temp can be exported, else by NCCL send/recv
- * (environment LCPP_MG_EXCHANGE=nccl forces it).  Equal keys keep
+ * engines, LCPP_MG_PULL_STREAMS streams per source, default 4) when every
+ * rank's temp can be exported, else by NCCL send/recv (environment
+ * LCPP_MG_EXCHANGE=nccl forces it).  Equal keys keep
  * their global input order.  Waits on `stream` for the exchange sizes (and
  * once more for the ranks' agreement on the IPC path); the rest is
  * asynchronous.  n_local, capacity < 2^32. */
